@@ -1,0 +1,163 @@
+// host.cpp -- error reporting, device caches, kernel attributes and TMA descriptors.
+//
+// The reference caches the opt-in shared-memory limit and the attribute call in unguarded
+// statics (cuda/volta_mma_attn.cu:34-57), which races when XLA calls handlers for several
+// devices from several threads.  Here every cache is guarded.
+#include "host.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <utility>
+
+namespace cfk {
+
+namespace {
+
+thread_local char t_last_error[512] = {0};
+
+constexpr int kMaxDevices = 64;
+std::once_flag g_dev_once[kMaxDevices];
+DeviceInfo g_dev_info[kMaxDevices];
+int g_dev_err[kMaxDevices];
+
+std::mutex g_attr_mu;
+std::set<std::pair<const void*, int>> g_attr_done;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+std::once_flag g_encode_once;
+EncodeTiledFn g_encode = nullptr;
+
+} // namespace
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+void clear_error() {
+    t_last_error[0] = '\0';
+}
+
+int current_device(DeviceInfo* info) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        return fail(CFK_ERR_LAUNCH, "cudaGetDevice: %s", cudaGetErrorString(e));
+    }
+    if (dev < 0 || dev >= kMaxDevices) {
+        return fail(CFK_ERR_UNSUPPORTED_DEVICE, "device ordinal %d out of range", dev);
+    }
+    std::call_once(g_dev_once[dev], [dev]() {
+        DeviceInfo d;
+        d.device = dev;
+        int major = 0, minor = 0;
+        cudaError_t r1 = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaError_t r2 = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        cudaError_t r3 = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaError_t r4 =
+            cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        d.cc = major * 10 + minor;
+        g_dev_err[dev] = (r1 || r2 || r3 || r4) ? 1 : 0;
+        g_dev_info[dev] = d;
+    });
+    if (g_dev_err[dev]) {
+        return fail(CFK_ERR_LAUNCH, "cannot query attributes of device %d", dev);
+    }
+    *info = g_dev_info[dev];
+    if (info->cc != 100) {
+        return fail(CFK_ERR_UNSUPPORTED_DEVICE,
+                    "device %d is sm_%d; this library holds sm_100a code only", dev, info->cc);
+    }
+    return CFK_OK;
+}
+
+int ensure_smem_attr(const void* kernel, int device, int bytes, const char* name) {
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    auto key = std::make_pair(kernel, device);
+    if (g_attr_done.count(key)) {
+        return CFK_OK;
+    }
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) {
+        return fail(CFK_ERR_LAUNCH, "%s: cudaFuncSetAttribute(%d bytes): %s", name, bytes,
+                    cudaGetErrorString(e));
+    }
+    g_attr_done.insert(key);
+    return CFK_OK;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        return fail(CFK_ERR_LAUNCH, "%s launch: %s", what, cudaGetErrorString(e));
+    }
+    return CFK_OK;
+}
+
+int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                 uint32_t b2, int swizzle_bytes, const char* what) {
+    std::call_once(g_encode_once, []() {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+        }
+    });
+    if (!g_encode) {
+        return fail(CFK_ERR_LAUNCH, "%s: driver has no cuTensorMapEncodeTiled", what);
+    }
+    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+    switch (swizzle_bytes) {
+    case 0:
+        sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+        break;
+    case 32:
+        sw = CU_TENSOR_MAP_SWIZZLE_32B;
+        break;
+    case 64:
+        sw = CU_TENSOR_MAP_SWIZZLE_64B;
+        break;
+    case 128:
+        sw = CU_TENSOR_MAP_SWIZZLE_128B;
+        break;
+    default:
+        return fail(CFK_ERR_INVALID_ARGUMENT, "%s: bad swizzle %d", what, swizzle_bytes);
+    }
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    cuuint32_t box[3] = {b0, b1, b2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        return fail(CFK_ERR_INVALID_ARGUMENT,
+                    "%s: cuTensorMapEncodeTiled failed (%d): dims %llu x %llu x %llu", what,
+                    static_cast<int>(r), static_cast<unsigned long long>(d0),
+                    static_cast<unsigned long long>(d1), static_cast<unsigned long long>(d2));
+    }
+    return CFK_OK;
+}
+
+} // namespace cfk
+
+extern "C" const char* cfk_last_error(void) {
+    return cfk::t_last_error;
+}
+
+extern "C" const char* cfk_version(void) {
+    return "colabfold-b200-kernels 0.1.0 (sm_100a)";
+}

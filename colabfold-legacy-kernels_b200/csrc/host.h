@@ -1,0 +1,61 @@
+// host.h -- host-side helpers shared by the C ABI entry points: error reporting, per-device
+// property caches, one-time kernel attributes and TMA tensor-map encoding.
+#pragma once
+
+#include <algorithm>
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "cfk.h"
+
+namespace cfk {
+
+// Records a printf-style message as the calling thread's last error and returns `code`.
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+
+// Clears the calling thread's last error.
+void clear_error();
+
+struct DeviceInfo {
+    int device = -1;
+    int cc = 0;        // major * 10 + minor
+    int num_sms = 0;
+    int max_smem_optin = 0;
+};
+
+// Looks up the current device (cached per device, thread-safe).  Fails with
+// CFK_ERR_UNSUPPORTED_DEVICE unless it is compute capability 10.0.
+int current_device(DeviceInfo* info);
+
+// Sets cudaFuncAttributeMaxDynamicSharedMemorySize once per (kernel, device).
+int ensure_smem_attr(const void* kernel, int device, int bytes, const char* name);
+
+// Maps cudaGetLastError() after a launch onto CFK_ERR_LAUNCH.
+int check_launch(const char* what);
+
+// TMA descriptor for a rank-3 tensor with dims (innermost first) d0, d1, d2 and byte strides of
+// dims 1 and 2; box b0 x b1 x b2; 16-bit elements; out-of-bounds elements read as zero.
+// swizzle_bytes is 0 (none), 32, 64 or 128.
+int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                 uint32_t b2, int swizzle_bytes, const char* what);
+
+// Argument checks shared by the attention entry points (dtype code, ranks, D in {8,16,32,64}).
+int check_attn_args(const char* fn, int dtype, int64_t N, int64_t H, int64_t Sq, int64_t Sk,
+                    int64_t D);
+
+inline bool aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+} // namespace cfk
+
+#define CFK_TRY(expr)                                                                              \
+    do {                                                                                           \
+        int cfk_rc_ = (expr);                                                                      \
+        if (cfk_rc_ != CFK_OK) {                                                                   \
+            return cfk_rc_;                                                                        \
+        }                                                                                          \
+    } while (0)

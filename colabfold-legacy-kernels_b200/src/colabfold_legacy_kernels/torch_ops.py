@@ -1,0 +1,140 @@
+"""PyTorch helpers over the C ABI: allocate outputs, pass device pointers and the current
+stream, and call the sm_100a kernels.  There is no fallback: a missing library or a non-B200
+device raises.
+
+These exist for tests, benchmarks and PyTorch users; XLA users go through the FFI handlers.
+"""
+
+import torch
+
+from . import cabi
+
+_DTYPES = {torch.float16: cabi.CFK_F16, torch.bfloat16: cabi.CFK_BF16}
+
+
+def _dtype_code(t):
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError("expected a float16 or bfloat16 tensor, got %s" % t.dtype) from None
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check(*ts):
+    for t in ts:
+        if t is not None:
+            if not t.is_cuda:
+                raise ValueError("tensors must be on a CUDA device")
+            if not t.is_contiguous():
+                raise ValueError("tensors must be contiguous")
+
+
+def attention_fwd(q, k, v, bias, kmask, scale, return_lse=True, out=None, lse=None):
+    """out [N,H,Sq,D] (and lse f32 [N,H,Sq]) of attention with pair bias and key mask."""
+    _check(q, k, v, bias, kmask)
+    n, h, sq, d = q.shape
+    sk = k.shape[2]
+    if out is None:
+        out = torch.empty_like(q)
+    if return_lse and lse is None:
+        lse = torch.empty((n, h, sq), dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        cabi.call("cfk_attn_fwd", _stream(q.device), _dtype_code(q), _ptr(q), _ptr(k), _ptr(v),
+                  _ptr(bias), _ptr(kmask), _ptr(out), _ptr(lse) if return_lse else None,
+                  n, h, sq, sk, d, float(scale))
+    return (out, lse) if return_lse else out
+
+
+def attention_bwd_workspace(n, h, sq, sk, d, device):
+    nbytes = cabi.workspace_size("cfk_attn_bwd_workspace_size", n, h, sq, sk, d)
+    return torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device)
+
+
+def attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=None, grads=None):
+    """(dq, dk, dv, dbias) of attention_fwd; dbias is f32 [H,Sq,Sk]."""
+    _check(q, k, v, bias, kmask, out, lse, dout)
+    n, h, sq, d = q.shape
+    sk = k.shape[2]
+    if grads is None:
+        grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
+                 torch.empty((h, sq, sk), dtype=torch.float32, device=q.device))
+    dq, dk, dv, dbias = grads
+    if workspace is None:
+        workspace = attention_bwd_workspace(n, h, sq, sk, d, q.device)
+    with torch.cuda.device(q.device):
+        cabi.call("cfk_attn_bwd", _stream(q.device), _dtype_code(q), _ptr(q), _ptr(k), _ptr(v),
+                  _ptr(bias), _ptr(kmask), _ptr(out), _ptr(lse), _ptr(dout), _ptr(dq), _ptr(dk),
+                  _ptr(dv), _ptr(dbias), _ptr(workspace), workspace.numel(), n, h, sq, sk, d,
+                  float(scale))
+    return dq, dk, dv, dbias
+
+
+def layer_norm_fwd(x, gamma, beta, eps, return_stats=False, out=None):
+    _check(x, gamma, beta)
+    m, c = x.shape
+    y = torch.empty_like(x) if out is None else out
+    mean = rstd = None
+    if return_stats:
+        mean = torch.empty(m, dtype=torch.float32, device=x.device)
+        rstd = torch.empty(m, dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        cabi.call("cfk_ln_fwd", _stream(x.device), _dtype_code(x), _ptr(x), _ptr(gamma),
+                  _ptr(beta), _ptr(y), _ptr(mean), _ptr(rstd), m, c, float(eps))
+    return (y, mean, rstd) if return_stats else y
+
+
+def layer_norm_bwd(x, gamma, dy, eps, mean=None, rstd=None, workspace=None):
+    """(dx, dgamma, dbeta); mean/rstd from layer_norm_fwd(return_stats=True) or recomputed."""
+    _check(x, gamma, dy, mean, rstd)
+    m, c = x.shape
+    dx = torch.empty_like(x)
+    dgamma = torch.empty(c, dtype=torch.float32, device=x.device)
+    dbeta = torch.empty(c, dtype=torch.float32, device=x.device)
+    if workspace is None:
+        nbytes = cabi.workspace_size("cfk_ln_bwd_workspace_size", m, c)
+        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        cabi.call("cfk_ln_bwd", _stream(x.device), _dtype_code(x), _ptr(x), _ptr(gamma),
+                  _ptr(mean), _ptr(rstd), _ptr(dy), _ptr(dx), _ptr(dgamma), _ptr(dbeta),
+                  _ptr(workspace), workspace.numel(), m, c, float(eps))
+    return dx, dgamma, dbeta
+
+
+def gdp_fwd(x, wp, bp, wg, bg, mask, out=None):
+    """mask[:,None] * (x@wp + bp) * sigmoid(x@wg + bg)."""
+    _check(x, wp, bp, wg, bg, mask)
+    m, k = x.shape
+    n = wp.shape[1]
+    if out is None:
+        out = torch.empty((m, n), dtype=x.dtype, device=x.device)
+    with torch.cuda.device(x.device):
+        cabi.call("cfk_gdp_fwd", _stream(x.device), _dtype_code(x), _ptr(x), _ptr(wp), _ptr(bp),
+                  _ptr(wg), _ptr(bg), _ptr(mask), _ptr(out), m, k, n)
+    return out
+
+
+def gdp_bwd(x, wp, bp, wg, bg, mask, dout, workspace=None):
+    """(dx, dwp, dbp, dwg, dbg); weight and bias gradients in f32."""
+    _check(x, wp, bp, wg, bg, mask, dout)
+    m, k = x.shape
+    n = wp.shape[1]
+    dx = torch.empty_like(x)
+    dwp = torch.empty((k, n), dtype=torch.float32, device=x.device)
+    dwg = torch.empty((k, n), dtype=torch.float32, device=x.device)
+    dbp = torch.empty(n, dtype=torch.float32, device=x.device)
+    dbg = torch.empty(n, dtype=torch.float32, device=x.device)
+    if workspace is None:
+        nbytes = cabi.workspace_size("cfk_gdp_bwd_workspace_size", m, k, n)
+        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        cabi.call("cfk_gdp_bwd", _stream(x.device), _dtype_code(x), _ptr(x), _ptr(wp), _ptr(bp),
+                  _ptr(wg), _ptr(bg), _ptr(mask), _ptr(dout), _ptr(dx), _ptr(dwp), _ptr(dbp),
+                  _ptr(dwg), _ptr(dbg), _ptr(workspace), workspace.numel(), m, k, n)
+    return dx, dwp, dbp, dwg, dbg

@@ -1,0 +1,148 @@
+/*
+ * cfk.h -- C ABI of the B200 (sm_100a) Evoformer kernels.
+ *
+ * This is the drop-in boundary beneath the XLA FFI handlers.  Every entry point takes raw
+ * device pointers, sizes, a dtype code and a CUDA stream; it validates its arguments, enqueues
+ * its kernels on that stream and returns.  No entry point synchronises, allocates device memory
+ * or creates streams, so every call can be recorded into a CUDA graph (XLA's command buffers).
+ * Scratch memory, where a kernel needs some, is passed in by the caller; its size comes from the
+ * matching *_workspace_size() query.
+ *
+ * Return value: CFK_OK (0) or one of the cfk_status codes; cfk_last_error() then gives a
+ * message for the failing call on the calling thread.
+ *
+ * Citations name the reference interface each entry point replaces
+ * (sokrypton/colabfold-legacy-kernels, path:line).
+ */
+#ifndef CFK_H_
+#define CFK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define CFK_API __attribute__((visibility("default")))
+#else
+#define CFK_API
+#endif
+
+/* A cudaStream_t; declared without the CUDA headers so this file stays plain C. */
+typedef struct CUstream_st* cfk_stream_t;
+
+/* Element type of the 16-bit tensors (q/k/v/out, x/y, weights).  The reference is F16 only. */
+typedef enum {
+    CFK_F16 = 0,
+    CFK_BF16 = 1,
+} cfk_dtype;
+
+typedef enum {
+    CFK_OK = 0,
+    CFK_ERR_INVALID_ARGUMENT = 1, /* bad shape, dtype, alignment or workspace size */
+    CFK_ERR_UNSUPPORTED_DEVICE = 2, /* the current device is not compute capability 10.0 */
+    CFK_ERR_LAUNCH = 3,             /* a CUDA launch or attribute call failed */
+} cfk_status;
+
+/* Message of the last failing call on this thread ("" if none). */
+CFK_API const char* cfk_last_error(void);
+
+/* Library version string. */
+CFK_API const char* cfk_version(void);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Attention with an additive pair bias and a key mask.                                       */
+/*                                                                                            */
+/*   logit[n,h,i,j] = scale * <q[n,h,i,:], k[n,h,j,:]> + bias[h,i,j]   if kmask[n,j] != 0     */
+/*                  = -1e4                                             otherwise (replaced,   */
+/*                                                                     bias dropped)          */
+/*   out[n,h,i,:]   = sum_j softmax_j(logit[n,h,i,:]) * v[n,h,j,:]                            */
+/*                                                                                            */
+/* Layouts (row-major, contiguous): q,out [N,H,Sq,D]; k,v [N,H,Sk,D]; bias [H,Sq,Sk] shared   */
+/* by all n; kmask u8 [N,Sk].  D in {8,16,32,64}.  fp32 accumulation and softmax.             */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Forward.  Replaces VoltaMma / VoltaWmma (cuda/volta_mma_attn.cu:304-351,
+ * cuda/volta_wmma_attn.cu:264-311).  lse may be NULL; otherwise it receives the natural-log
+ * log-sum-exp of each row, f32 [N,H,Sq], which the backward needs. */
+CFK_API int cfk_attn_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* q, const void* k,
+                 const void* v, const void* bias, const uint8_t* kmask, void* out, float* lse,
+                 int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D, float scale);
+
+/* Bytes of scratch memory cfk_attn_bwd needs for these sizes. */
+CFK_API int cfk_attn_bwd_workspace_size(int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                size_t* bytes);
+
+/* Backward (no counterpart in the reference, which is forward-only; it is the autodiff of
+ * cuda/volta_mma_attn.cu:139-271).  Inputs are the forward's inputs plus out, its lse and dout.
+ * Outputs: dq [N,H,Sq,D], dk, dv [N,H,Sk,D] in dtype; dbias f32 [H,Sq,Sk] = sum over n of
+ * dlogit (zero where masked).  Masked logits are constants, so they pass no gradient. */
+CFK_API int cfk_attn_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* q, const void* k,
+                 const void* v, const void* bias, const uint8_t* kmask, const void* out,
+                 const float* lse, const void* dout, void* dq, void* dk, void* dv, float* dbias,
+                 void* workspace, size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq,
+                 int64_t Sk, int64_t D, float scale);
+
+/* ------------------------------------------------------------------------------------------ */
+/* LayerNorm over the last axis: y = (x - mean) * rstd * gamma + beta,                        */
+/* rstd = 1/sqrt(var + eps).  x, y [M,C] in dtype; gamma, beta f32 [C]; statistics in f32.    */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Forward.  Replaces VoltaLayerNorm (cuda/volta_ops.cu:62-95).  mean and rstd (f32 [M]) may be
+ * NULL; when given they receive the row statistics for the backward. */
+CFK_API int cfk_ln_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, const float* gamma,
+               const float* beta, void* y, float* mean, float* rstd, int64_t M, int64_t C,
+               float eps);
+
+/* Bytes of scratch memory cfk_ln_bwd needs. */
+CFK_API int cfk_ln_bwd_workspace_size(int64_t M, int64_t C, size_t* bytes);
+
+/* Backward (no counterpart in the reference; autodiff of cuda/volta_ops.cu:40-58).
+ * mean/rstd may be NULL, in which case they are recomputed from x.  Outputs dx [M,C] in dtype,
+ * dgamma, dbeta f32 [C] (written, not accumulated). */
+CFK_API int cfk_ln_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, const float* gamma,
+               const float* mean, const float* rstd, const void* dy, void* dx, float* dgamma,
+               float* dbeta, void* workspace, size_t workspace_bytes, int64_t M, int64_t C,
+               float eps);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Gated dual projection:                                                                     */
+/*   out[m,n] = mask[m] * (x@wp + bp)[m,n] * sigmoid((x@wg + bg)[m,n])                        */
+/* x [M,K], wp, wg [K,N] row-major, bp, bg [N], mask [M], out [M,N]; all in dtype.            */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Forward.  Replaces VoltaGdp / VoltaGdpWmma (cuda/volta_ops.cu:210-265,
+ * cuda/volta_gdp_wmma.cu:99-140).  N must be a multiple of 8, as in the reference. */
+CFK_API int cfk_gdp_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, const void* wp,
+                const void* bp, const void* wg, const void* bg, const void* mask, void* out,
+                int64_t M, int64_t K, int64_t N);
+
+/* Bytes of scratch memory cfk_gdp_bwd needs. */
+CFK_API int cfk_gdp_bwd_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes);
+
+/* Backward (no counterpart in the reference; autodiff of cuda/volta_ops.cu:185-207 with mask
+ * treated as a constant).  Outputs dx [M,K] in dtype; dwp, dwg f32 [K,N]; dbp, dbg f32 [N]. */
+CFK_API int cfk_gdp_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, const void* wp,
+                const void* bp, const void* wg, const void* bg, const void* mask,
+                const void* dout, void* dx, float* dwp, float* dbp, float* dwg, float* dbg,
+                void* workspace, size_t workspace_bytes, int64_t M, int64_t K, int64_t N);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Diagnostics (no counterpart in the reference).                                             */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Every wait inside a kernel (on a barrier or on the tensor-memory pipeline) gives up after
+ * about one second.  It then records a code in a per-device status word and the kernel returns
+ * early instead of hanging.  This reads the word of the current device (0 = no timeout seen). */
+CFK_API int cfk_device_status(uint32_t* code);
+
+/* Clears the status word of the current device. */
+CFK_API int cfk_clear_device_status(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* CFK_H_ */

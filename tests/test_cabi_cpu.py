@@ -1,0 +1,80 @@
+"""The C ABI library, without a GPU: it loads, exports exactly the functions include/cfk.h
+declares, depends on the C library only (the reference's ldd audit,
+.github/workflows/build-and-publish.yml:53-64), and rejects bad arguments before it touches a
+device.
+"""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def _declared():
+    text = (REPO / "include" / "cfk.h").read_text()
+    return sorted(set(re.findall(r"CFK_API\s+[\w\s\*]+?\b(cfk_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def libpath():
+    import colabfold_legacy_kernels as clk
+    try:
+        return clk.c_library_path(100)
+    except FileNotFoundError:
+        pytest.fail("libcfk_sm100.so is not built; run colabfold-legacy-kernels_b200/build.py")
+
+
+def test_header_declares_the_c_abi():
+    names = _declared()
+    for n in ("cfk_attn_fwd", "cfk_attn_bwd", "cfk_attn_bwd_workspace_size", "cfk_ln_fwd",
+              "cfk_ln_bwd", "cfk_ln_bwd_workspace_size", "cfk_gdp_fwd", "cfk_gdp_bwd",
+              "cfk_gdp_bwd_workspace_size", "cfk_last_error", "cfk_version",
+              "cfk_device_status", "cfk_clear_device_status"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(libpath):
+    lib = ctypes.CDLL(libpath)
+    missing = [n for n in _declared() if not hasattr(lib, n)]
+    assert not missing, "not exported: %s" % missing
+    out = subprocess.run(["nm", "-D", "--defined-only", libpath], capture_output=True,
+                         text=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
+    extra = {s for s in exported if not s.startswith("__cudaRegisterLinkedBinary")} - set(_declared())
+    assert not extra, "unexpected exports: %s" % sorted(extra)
+
+
+def test_library_links_libc_only(libpath):
+    out = subprocess.run(["ldd", libpath], capture_output=True, text=True).stdout
+    assert not re.search(r"libcudart|libstdc\+\+|libgcc_s|libcuda\.so", out), out
+
+
+def test_signatures_match_binding():
+    from colabfold_legacy_kernels import cabi
+    assert set(cabi.SIGNATURES) | {"cfk_last_error", "cfk_version"} == set(_declared())
+
+
+def test_bad_arguments_rejected_without_device(libpath):
+    from colabfold_legacy_kernels import cabi
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_attn_fwd", None, 7, None, None, None, None, None, None, None,
+                  1, 1, 1, 1, 32, 1.0)
+    assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT and "dtype" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_attn_fwd", None, cabi.CFK_BF16, None, None, None, None, None, None, None,
+                  1, 1, 1, 1, 48, 1.0)
+    assert "head dim" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_ln_fwd", None, cabi.CFK_BF16, None, None, None, None, None, None,
+                  4, 0, 1e-5)
+    assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT
+    assert "sm_100a" in cabi.version()
+
+
+def test_workspace_queries_need_no_device(libpath):
+    from colabfold_legacy_kernels import cabi
+    assert cabi.workspace_size("cfk_ln_bwd_workspace_size", 1 << 20, 128) > 0
