@@ -106,7 +106,7 @@ int check_launch(const char* what) {
 
 int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                  uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
-                 uint32_t b2, int swizzle_bytes, const char* what) {
+                 uint32_t b2, int swizzle_bytes, const char* what, bool f32) {
     std::call_once(g_encode_once, []() {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -140,7 +140,7 @@ int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, u
     cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
     cuuint32_t box[3] = {b0, b1, b2};
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims,
+    CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims,
                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {

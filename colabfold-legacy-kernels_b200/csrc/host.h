@@ -40,7 +40,7 @@ int check_launch(const char* what);
 // swizzle_bytes is 0 (none), 32, 64 or 128.
 int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                  uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
-                 uint32_t b2, int swizzle_bytes, const char* what);
+                 uint32_t b2, int swizzle_bytes, const char* what, bool f32 = false);
 
 // Argument checks shared by the attention entry points (dtype code, ranks, D in {8,16,32,64}).
 int check_attn_args(const char* fn, int dtype, int64_t N, int64_t H, int64_t Sq, int64_t Sk,

@@ -128,6 +128,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
                  : "memory");
 }
 
+// Tiled add-reduction of a shared-memory box into global memory through a tensor map (f32 map:
+// element-wise f32 add, performed at L2).  Completes through the issuing thread's bulk group.
+// Out-of-range parts of the box are skipped.  Coordinates must not be negative.
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src,
+                                                  int32_t c0, int32_t c1, int32_t c2) {
+    asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group"
+                 " [%0, {%2, %3, %4}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
 // Bulk (untiled) add-reduction of f32 data from shared into global memory, completed through
 // the bulk async-group of the issuing thread.  Both addresses 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_reduce_add_f32(float* gdst, const void* ssrc,
