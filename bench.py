@@ -1,0 +1,472 @@
+"""Benchmark of the B200 Evoformer kernels -- prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE.json metric "tri-attn fwd+bwd TFLOP/s @N_res=768 ..."): one step is the
+triangle-attention (starting node) forward + backward with pair bias and key mask at
+N_res = 768, H = 4, d = 32, bf16 (config C3): out, lse = attn_fwd(q, k, v, bias, kmask);
+dq, dk, dv, dbias = attn_bwd(...).  The 768 attention rows are sharded across the N GPUs
+(strong scaling); every GPU holds the full bias and the per-GPU dbias partials are summed with
+one NCCL all-reduce per step.  Inputs are synthetic, drawn from seeded generators with the
+configuration's shapes and distributions (oracle/configs.py), and resident in HBM.
+
+value      = 695.8 GFLOP (algorithmic fwd+bwd flops of the whole job) / ms_per_step
+e2e        = the same metric through the C ABI with pinned host buffers: every step copies
+             q, k, v, bias, kmask, dout host->device and out, dq, dk, dv, dbias device->host
+roofline   = the dominant kernel (the backward main kernel), achieved TFLOP/s from CUDA events
+             around its launches against the measured sustained bf16 peak
+cpu_baseline = the CPU oracle (torch, fp32, all host threads) on a bounded sample of rows
+Also reported: LayerNorm forward HBM GB/s and the gated dual projection on config C4.
+
+--impl reference times the reference's CPU path for this workload: the reference ships GPU
+kernels for sm_70/sm_75 only and no CPU implementation, so its semantics restated on the CPU
+(oracle/, torch fp32, all host threads) stand in, on a bounded sample of rows per step.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "colabfold-legacy-kernels_b200" / "src"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "tri-attn fwd+bwd TFLOP/s @N_res=768"
+UNIT = "TFLOP/s"
+N_RES, HEADS, HEAD_DIM = 768, 4, 32
+
+
+def attn_flops(n, h, s, d):
+    return 12 * n * h * s * s * d  # 4 n h s^2 d forward + 8 n h s^2 d backward
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        j = json.loads(p.read_text())
+        return {"hbm_gbs": j["hbm_gbs"], "bf16": j["bf16_tflops"],
+                "bf16_sustained": j.get("bf16_tflops_sustained", j["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def traffic_from_profiles(key):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary, if one exists."""
+    p = REPO / "profiles" / "traffic.json"
+    if p.is_file():
+        try:
+            return json.loads(p.read_text()).get(key)
+        except (ValueError, OSError):
+            return None
+    return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU legs (oracle): the reference arm and the cpu_baseline field
+# ------------------------------------------------------------------------------------------
+def cpu_attention_sample(inputs_cpu, rows, reps=1):
+    """Times the oracle's fp32 forward + backward on `rows` attention rows; returns
+    (seconds per rep, flops per rep, threads)."""
+    import torch
+    import oracle
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    q, k, v, bias, kmask, dout = (inputs_cpu[x][:rows] if x not in ("bias",) else inputs_cpu[x]
+                                  for x in ("q", "k", "v", "bias", "kmask", "dout"))
+    scale = inputs_cpu["scale"]
+    f32 = torch.float32
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        out, lse = oracle.attention_fwd_chunked(q, k, v, bias, kmask, scale, dtype=f32, chunk=4)
+        for r0 in range(0, rows, 4):
+            sl = slice(r0, r0 + 4)
+            oracle.attention_bwd(q[sl], k[sl], v[sl], bias, kmask[sl], out[sl], lse[sl],
+                                 dout[sl], scale, dtype=f32)
+        times.append(time.perf_counter() - t0)
+    n, h, s, d = q.shape
+    return statistics.median(times), attn_flops(n, h, s, d), torch.get_num_threads()
+
+
+def cpu_sample_inputs(rows):
+    import oracle
+    cfg = oracle.configs.C3
+    # the same generator as the GPU run, on the CPU, for the first `rows` rows
+    small = oracle.configs.AttnConfig(cfg.name, rows, cfg.h, cfg.s, cfg.d, cfg.seed, True,
+                                      cfg.mask, cfg.from_pair)
+    return oracle.configs.make_attention_inputs(small, device="cpu")
+
+
+def run_reference(args, rank):
+    """--impl reference: the CPU restatement, rank 0 only."""
+    if rank != 0:
+        return None
+    rows = args.cpu_rows
+    inputs = cpu_sample_inputs(rows)
+    for _ in range(max(1, args.warmup)):
+        cpu_attention_sample(inputs, rows)
+    secs = []
+    flops = None
+    threads = None
+    for _ in range(args.steps):
+        t, flops, threads = cpu_attention_sample(inputs, rows)
+        secs.append(t)
+    sec = statistics.median(secs)
+    value = flops / sec / 1e12
+    sample = "%d of %d attention rows of config C3 (fwd+bwd, fp32 torch on %d threads)" % (
+        rows, N_RES, threads)
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3 * (N_RES / rows), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "tri_start_768 fwd+bwd (C3)", "n_res": N_RES, "heads": HEADS,
+                   "head_dim": HEAD_DIM, "sample_rows": rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference has no CPU implementation and its GPU kernels are sm_70/sm_75 "
+                "only; its semantics restated in oracle/ (torch CPU) are timed instead",
+    }
+
+
+# ------------------------------------------------------------------------------------------
+# GPU leg
+# ------------------------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import oracle
+    from colabfold_legacy_kernels import torch_ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = oracle.configs.C3
+    full = oracle.configs.make_attention_inputs(cfg, device=dev)
+    r0 = rank * N_RES // world
+    r1 = (rank + 1) * N_RES // world
+    if args.rows:
+        r1 = r0 + args.rows  # profiling: a subset of the rows
+    q, k, v, dout, kmask = (full[x][r0:r1].contiguous() for x in ("q", "k", "v", "dout", "kmask"))
+    bias, scale = full["bias"], full["scale"]
+    del full
+    n = r1 - r0
+    out = torch.empty_like(q)
+    lse = torch.empty((n, HEADS, N_RES), dtype=torch.float32, device=dev)
+    grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
+             torch.empty((HEADS, N_RES, N_RES), dtype=torch.float32, device=dev))
+    ws = torch_ops.attention_bwd_workspace(n, HEADS, N_RES, N_RES, HEAD_DIM, dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    comm = torch.cuda.Stream(dev) if world > 1 else None
+
+    ev = {name: [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+          for name in ("step", "fwd", "bwd_main")}
+
+    def step(record=False):
+        stream = torch.cuda.current_stream(dev)
+        if record:
+            ev["step"][0].record(stream)
+            ev["fwd"][0].record(stream)
+        torch_ops.attention_fwd(q, k, v, bias, kmask, scale, out=out, lse=lse)
+        if record:
+            ev["fwd"][1].record(stream)
+        torch_ops.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=ws,
+                                grads=grads, phase=0)
+        if record:
+            ev["bwd_main"][0].record(stream)
+        torch_ops.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=ws,
+                                grads=grads, phase=1)
+        if record:
+            ev["bwd_main"][1].record(stream)
+        if world > 1:
+            # dbias is final after the main kernel: reduce it while the converts run
+            comm.wait_stream(stream)
+            with torch.cuda.stream(comm):
+                dist.all_reduce(grads[3])
+        torch_ops.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=ws,
+                                grads=grads, phase=2)
+        if world > 1:
+            stream.wait_stream(comm)
+        if record:
+            ev["step"][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    step_ms, fwd_ms, bwd_ms = [], [], []
+    with ClockSampler(local_rank) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        wall0 = time.perf_counter()
+        for _ in range(args.steps):
+            flush.zero_()  # untimed: evicts L2 between steps
+            step(record=True)
+            torch.cuda.synchronize()
+            step_ms.append(ev["step"][0].elapsed_time(ev["step"][1]))
+            fwd_ms.append(ev["fwd"][0].elapsed_time(ev["fwd"][1]))
+            bwd_ms.append(ev["bwd_main"][0].elapsed_time(ev["bwd_main"][1]))
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        wall = time.perf_counter() - wall0
+    ms = sum(step_ms) / len(step_ms)
+    ms_fwd = sum(fwd_ms) / len(fwd_ms)
+    ms_bwd = sum(bwd_ms) / len(bwd_ms)
+    if world > 1:
+        t = torch.tensor([ms, ms_fwd, ms_bwd], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_fwd, ms_bwd = t.tolist()
+    total_flops = attn_flops(N_RES, HEADS, N_RES, HEAD_DIM)
+    value = total_flops / (ms * 1e-3) / 1e12
+
+    if args.profile:
+        return {"profile": True, "rows": n, "ms_per_step": ms, "ms_fwd": ms_fwd, "ms_bwd": ms_bwd}
+
+    # ---------------- end to end through the C ABI with host buffers ----------------
+    host = {x: torch.empty_like(t, device="cpu").pin_memory()
+            for x, t in (("q", q), ("k", k), ("v", v), ("dout", dout), ("kmask", kmask),
+                         ("bias", bias))}
+    for x, t in (("q", q), ("k", k), ("v", v), ("dout", dout), ("kmask", kmask), ("bias", bias)):
+        host[x].copy_(t)
+    host_out = {x: torch.empty_like(t, device="cpu").pin_memory()
+                for x, t in (("out", out), ("dq", grads[0]), ("dk", grads[1]), ("dv", grads[2]),
+                             ("dbias", grads[3]))}
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_out.values())
+    e2e_ms = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(args.e2e_steps + 1):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for x, t in (("q", q), ("k", k), ("v", v), ("dout", dout), ("kmask", kmask),
+                     ("bias", bias)):
+            t.copy_(host[x], non_blocking=True)
+        step()
+        for x, t in (("out", out), ("dq", grads[0]), ("dk", grads[1]), ("dv", grads[2]),
+                     ("dbias", grads[3])):
+            host_out[x].copy_(t, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        if i > 0:  # the first is a warm-up
+            e2e_ms.append(e0.elapsed_time(e1))
+    me2e = sum(e2e_ms) / len(e2e_ms)
+    if world > 1:
+        t = torch.tensor([me2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        me2e = t.item()
+        h2d_t = torch.tensor([h2d, d2h], device=dev, dtype=torch.float64)
+        dist.all_reduce(h2d_t)
+        h2d, d2h = (int(x) for x in h2d_t.tolist())
+    e2e_value = total_flops / (me2e * 1e-3) / 1e12
+
+    pk = peaks()
+    bwd_flops_launch = 8 * n * HEADS * N_RES * N_RES * HEAD_DIM
+    achieved = bwd_flops_launch / (ms_bwd * 1e-3) / 1e12
+    roofline = {
+        "kernel": "attn_bwd_kernel<bf16, D=32> (cfk_attn_bwd phase 1)",
+        "bound": "tensor", "achieved": achieved, "peak": pk["bf16_sustained"],
+        "unit": "TFLOP/s", "frac": achieved / pk["bf16_sustained"],
+        "peak_source": pk["source"] + " bf16_tflops_sustained",
+        "traffic": traffic_from_profiles("attn_bwd_tri768"),
+        "flops_per_launch": bwd_flops_launch,
+        "ms_per_launch": ms_bwd,
+        "fwd_kernel": {"achieved": 4 * n * HEADS * N_RES * N_RES * HEAD_DIM / (ms_fwd * 1e-3) / 1e12,
+                       "ms_per_launch": ms_fwd, "unit": "TFLOP/s"},
+    }
+    result = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "tri_start_768 fwd+bwd (C3)", "n_res": N_RES, "heads": HEADS,
+                   "head_dim": HEAD_DIM, "rows_per_gpu": n, "parallelism": "rows%d" % world,
+                   "l2": "flushed between steps (256 MB write, outside the timed events)"},
+        "gpu_launches": 6 * args.steps,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": me2e},
+        "roofline": roofline,
+        "clocks": clocks.summary(),
+        "wall_s_timed": wall,
+    }
+    if world == 1 and not args.skip_extras:
+        result["layernorm"] = bench_layernorm(dev, pk)
+    return result
+
+
+def bench_layernorm(dev, pk, steps=20):
+    """LayerNorm forward and backward on config C4 (M = 1024*1024, C = 128, bf16)."""
+    import torch
+    import oracle
+    from colabfold_legacy_kernels import torch_ops
+    inp = oracle.configs.make_ln_gdp_inputs(oracle.configs.C4, device=dev)
+    x, gamma, beta, dy = inp["x"], inp["gamma"], inp["beta"], inp["dy"]
+    m, c = x.shape
+    y = torch.empty_like(x)
+    mean = torch.empty(m, device=dev)
+    rstd = torch.empty(m, device=dev)
+    res = {}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        torch_ops.layer_norm_fwd(x, gamma, beta, 1e-5, out=y)
+    fwd = []
+    for _ in range(steps):
+        e0.record()
+        torch_ops.layer_norm_fwd(x, gamma, beta, 1e-5, out=y)
+        e1.record()
+        torch.cuda.synchronize()
+        fwd.append(e0.elapsed_time(e1))
+    ms = statistics.median(fwd)
+    gbs = oracle.layer_norm.bytes_fwd(m, c) / (ms * 1e-3) / 1e9
+    res["fwd"] = {"metric": "LayerNorm fwd HBM GB/s [1M x 128] bf16", "value": gbs, "unit": "GB/s",
+                  "ms": ms, "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"],
+                                         "unit": "GB/s", "frac": gbs / pk["hbm_gbs"],
+                                         "traffic": traffic_from_profiles("ln_fwd_c4")}}
+    y, mean, rstd = torch_ops.layer_norm_fwd(x, gamma, beta, 1e-5, return_stats=True)
+    ws = torch.empty(1 << 22, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        torch_ops.layer_norm_bwd(x, gamma, dy, 1e-5, mean=mean, rstd=rstd, workspace=ws)
+    bwd = []
+    for _ in range(steps):
+        e0.record()
+        torch_ops.layer_norm_bwd(x, gamma, dy, 1e-5, mean=mean, rstd=rstd, workspace=ws)
+        e1.record()
+        torch.cuda.synchronize()
+        bwd.append(e0.elapsed_time(e1))
+    ms = statistics.median(bwd)
+    gbs = oracle.layer_norm.bytes_bwd(m, c) / (ms * 1e-3) / 1e9
+    res["bwd"] = {"metric": "LayerNorm bwd HBM GB/s [1M x 128] bf16", "value": gbs,
+                  "unit": "GB/s", "ms": ms, "roofline": {"bound": "hbm", "achieved": gbs,
+                                                         "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                                         "frac": gbs / pk["hbm_gbs"]}}
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-rows", type=int, default=32,
+                    help="attention rows in one CPU sample (reference arm and cpu_baseline)")
+    ap.add_argument("--skip-extras", action="store_true", help="skip LayerNorm/GDP lines")
+    ap.add_argument("--skip-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="profiling only: attention rows on this GPU instead of 768/N")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling only: time the attention steps and stop (no e2e/extras/cpu)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            sys.exit("bench.py: --gpus %d needs torchrun with %d processes" % (args.gpus, args.gpus))
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        res = run_ours(args, rank, world, local_rank)
+        if rank == 0 and world == 1 and not args.skip_cpu and not args.profile:
+            # size the sample to ~5 s per repetition (3 repetitions, ~15 s of CPU work)
+            probe = cpu_sample_inputs(8)
+            t8, _, _ = cpu_attention_sample(probe, 8)
+            rows = int(max(8, min(N_RES, 8 * 5.0 / max(t8, 1e-3))))
+            inputs = cpu_sample_inputs(rows)
+            sec, flops, threads = cpu_attention_sample(inputs, rows, reps=3)
+            res["cpu_baseline"] = {
+                "value": flops / sec / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": "%d of %d rows of C3 fwd+bwd, oracle/ fp32 torch, median of 3 (%.2f s)"
+                          % (rows, N_RES, sec)}
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -671,7 +671,7 @@ template <typename T, int D, bool kBiasTma>
 int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                const void* v, const void* bias, const uint8_t* kmask, const void* out,
                const float* lse, const void* dout, void* dq, void* dk, void* dv, float* dbias,
-               uint8_t* ws, int N, int H, int Sq, int Sk, float scale) {
+               uint8_t* ws, int N, int H, int Sq, int Sk, float scale, int phases) {
     using C = BwdCfg<D>;
     using G = Geo<D>;
     const BwdWorkspace wl = bwd_workspace(N, H, Sq, Sk, D);
@@ -725,24 +725,29 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
     p.mask_bits = mask_bias_bits(scale);
     p.dbias_atomic = p.n_bc > 1 ? 1 : 0;
 
-    const size_t acc_bytes = wl.delta_off;
-    if (cudaMemsetAsync(ws, 0, acc_bytes, st) != cudaSuccess ||
-        (p.dbias_atomic &&
-         cudaMemsetAsync(dbias, 0, static_cast<size_t>(H) * Sq * Sk * 4, st) != cudaSuccess)) {
-        return fail(CFK_ERR_LAUNCH, "cfk_attn_bwd: memset failed");
-    }
     const int64_t rows = static_cast<int64_t>(N) * H * Sq;
-    attn_bwd_delta_kernel<T, D><<<static_cast<int>((rows + 255) / 256), 256, 0, st>>>(
-        static_cast<const T*>(out), static_cast<const T*>(dout), delta, rows);
-    CFK_TRY(check_launch("attn_bwd_delta"));
-
-    auto kern = attn_bwd_kernel<T, D, kBiasTma>;
-    CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, C::kSmemBytes,
-                             "attn_bwd"));
-    const int grid = static_cast<int>(std::min<int64_t>(p.items, dev.num_sms));
-    kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, tb, tdq, tdk, tdv, p);
-    CFK_TRY(check_launch("attn_bwd"));
-
+    if (phases & 1) {
+        const size_t acc_bytes = wl.delta_off;
+        if (cudaMemsetAsync(ws, 0, acc_bytes, st) != cudaSuccess ||
+            (p.dbias_atomic &&
+             cudaMemsetAsync(dbias, 0, static_cast<size_t>(H) * Sq * Sk * 4, st) != cudaSuccess)) {
+            return fail(CFK_ERR_LAUNCH, "cfk_attn_bwd: memset failed");
+        }
+        attn_bwd_delta_kernel<T, D><<<static_cast<int>((rows + 255) / 256), 256, 0, st>>>(
+            static_cast<const T*>(out), static_cast<const T*>(dout), delta, rows);
+        CFK_TRY(check_launch("attn_bwd_delta"));
+    }
+    if (phases & 2) {
+        auto kern = attn_bwd_kernel<T, D, kBiasTma>;
+        CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, C::kSmemBytes,
+                                 "attn_bwd"));
+        const int grid = static_cast<int>(std::min<int64_t>(p.items, dev.num_sms));
+        kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, tb, tdq, tdk, tdv, p);
+        CFK_TRY(check_launch("attn_bwd"));
+    }
+    if (!(phases & 4)) {
+        return CFK_OK;
+    }
     const int cgrid = dev.num_sms * 8;
     f32_to_16_kernel<T><<<cgrid, 256, 0, st>>>(dq_acc, static_cast<T*>(dq), rows * D / 8);
     const int64_t kv8 = static_cast<int64_t>(N) * H * Sk * D / 8;
@@ -755,14 +760,16 @@ template <typename T>
 int dispatch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                  const void* v, const void* bias, const uint8_t* kmask, const void* out,
                  const float* lse, const void* dout, void* dq, void* dk, void* dv, float* dbias,
-                 uint8_t* ws, int N, int H, int Sq, int Sk, int D, float scale) {
+                 uint8_t* ws, int N, int H, int Sq, int Sk, int D, float scale, int phases) {
     const bool bias_tma = (Sk % 8 == 0) && aligned16(bias);
 #define CFK_BWD_D(DD)                                                                              \
     if (D == DD) {                                                                                 \
         return bias_tma ? launch_bwd<T, DD, true>(st, dev, q, k, v, bias, kmask, out, lse, dout,   \
-                                                  dq, dk, dv, dbias, ws, N, H, Sq, Sk, scale)      \
+                                                  dq, dk, dv, dbias, ws, N, H, Sq, Sk, scale,      \
+                                                  phases)                                          \
                         : launch_bwd<T, DD, false>(st, dev, q, k, v, bias, kmask, out, lse, dout,  \
-                                                   dq, dk, dv, dbias, ws, N, H, Sq, Sk, scale);    \
+                                                   dq, dk, dv, dbias, ws, N, H, Sq, Sk, scale,     \
+                                                   phases);                                        \
     }
     CFK_BWD_D(8)
     CFK_BWD_D(16)
@@ -789,17 +796,23 @@ extern "C" int cfk_attn_bwd_workspace_size(int64_t N, int64_t H, int64_t Sq, int
     return CFK_OK;
 }
 
-extern "C" int cfk_attn_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* q, const void* k,
-                            const void* v, const void* bias, const uint8_t* kmask,
-                            const void* out, const float* lse, const void* dout, void* dq,
-                            void* dk, void* dv, float* dbias, void* workspace,
-                            size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq, int64_t Sk,
-                            int64_t D, float scale) {
+namespace {
+
+// Shared body of cfk_attn_bwd (phases = 7) and cfk_attn_bwd_phase (one bit).
+int attn_bwd_entry(const char* fn, int phases, cfk_stream_t stream, cfk_dtype dtype,
+                   const void* q, const void* k, const void* v, const void* bias,
+                   const uint8_t* kmask, const void* out, const float* lse, const void* dout,
+                   void* dq, void* dk, void* dv, float* dbias, void* workspace,
+                   size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                   float scale) {
     clear_error();
-    CFK_TRY(check_attn_args("cfk_attn_bwd", dtype, N, H, Sq, Sk, D));
+    CFK_TRY(check_attn_args(fn, dtype, N, H, Sq, Sk, D));
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (H == 0 || Sq == 0 || Sk == 0 || N == 0) {
         // Empty: gradients are zero (dq for Sk == 0; dk, dv for Sq == 0; dbias always).
+        if (!(phases & 4)) {
+            return CFK_OK;
+        }
         cudaError_t e = cudaSuccess;
         if (dbias && H * Sq * Sk > 0) {
             e = cudaMemsetAsync(dbias, 0, static_cast<size_t>(H * Sq * Sk) * 4, st);
@@ -815,21 +828,21 @@ extern "C" int cfk_attn_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* q,
                 e = cudaMemsetAsync(dv, 0, static_cast<size_t>(N * H * Sk * D) * 2, st);
             }
         }
-        return e == cudaSuccess ? CFK_OK : fail(CFK_ERR_LAUNCH, "cfk_attn_bwd: memset failed");
+        return e == cudaSuccess ? CFK_OK : fail(CFK_ERR_LAUNCH, "%s: memset failed", fn);
     }
     if (!q || !k || !v || !bias || !kmask || !out || !lse || !dout || !dq || !dk || !dv ||
         !dbias) {
-        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_attn_bwd: null buffer");
+        return fail(CFK_ERR_INVALID_ARGUMENT, "%s: null buffer", fn);
     }
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(dout) ||
         !aligned16(dq) || !aligned16(dk) || !aligned16(dv)) {
         return fail(CFK_ERR_INVALID_ARGUMENT,
-                    "cfk_attn_bwd: q, k, v, out, dout, dq, dk and dv must be 16-byte aligned");
+                    "%s: q, k, v, out, dout, dq, dk and dv must be 16-byte aligned", fn);
     }
     const size_t need = attn::bwd_workspace(N, H, Sq, Sk, D).total;
     if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) {
         return fail(CFK_ERR_INVALID_ARGUMENT,
-                    "cfk_attn_bwd: workspace must be 256-byte aligned and hold %zu bytes (got %zu)",
+                    "%s: workspace must be 256-byte aligned and hold %zu bytes (got %zu)", fn,
                     need, workspace_bytes);
     }
     DeviceInfo dev;
@@ -839,7 +852,36 @@ extern "C" int cfk_attn_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* q,
               sk = static_cast<int>(Sk), d = static_cast<int>(D);
     return dtype == CFK_BF16
                ? attn::dispatch_bwd<__nv_bfloat16>(st, dev, q, k, v, bias, kmask, out, lse, dout,
-                                                   dq, dk, dv, dbias, ws, n, h, sq, sk, d, scale)
+                                                   dq, dk, dv, dbias, ws, n, h, sq, sk, d, scale,
+                                                   phases)
                : attn::dispatch_bwd<__half>(st, dev, q, k, v, bias, kmask, out, lse, dout, dq, dk,
-                                            dv, dbias, ws, n, h, sq, sk, d, scale);
+                                            dv, dbias, ws, n, h, sq, sk, d, scale, phases);
+}
+
+} // namespace
+
+extern "C" int cfk_attn_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* q, const void* k,
+                            const void* v, const void* bias, const uint8_t* kmask,
+                            const void* out, const float* lse, const void* dout, void* dq,
+                            void* dk, void* dv, float* dbias, void* workspace,
+                            size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq, int64_t Sk,
+                            int64_t D, float scale) {
+    return attn_bwd_entry("cfk_attn_bwd", 7, stream, dtype, q, k, v, bias, kmask, out, lse, dout,
+                          dq, dk, dv, dbias, workspace, workspace_bytes, N, H, Sq, Sk, D, scale);
+}
+
+extern "C" int cfk_attn_bwd_phase(int phase, cfk_stream_t stream, cfk_dtype dtype,
+                                  const void* q, const void* k, const void* v, const void* bias,
+                                  const uint8_t* kmask, const void* out, const float* lse,
+                                  const void* dout, void* dq, void* dk, void* dv, float* dbias,
+                                  void* workspace, size_t workspace_bytes, int64_t N, int64_t H,
+                                  int64_t Sq, int64_t Sk, int64_t D, float scale) {
+    if (phase < 0 || phase > 2) {
+        clear_error();
+        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_attn_bwd_phase: phase %d not in {0,1,2}",
+                    phase);
+    }
+    return attn_bwd_entry("cfk_attn_bwd_phase", 1 << phase, stream, dtype, q, k, v, bias, kmask,
+                          out, lse, dout, dq, dk, dv, dbias, workspace, workspace_bytes, N, H, Sq,
+                          Sk, D, scale);
 }

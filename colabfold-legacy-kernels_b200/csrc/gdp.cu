@@ -1,0 +1,1250 @@
+// gdp.cu -- gated dual projection, forward and backward.
+//
+//   out[m, n] = mask[m] * (x @ wp + bp)[m, n] * sigmoid((x @ wg + bg)[m, n])
+//
+// after volta_gdp_kernel (cuda/volta_ops.cu:109-208) and volta_gdp_wmma_kernel
+// (cuda/volta_gdp_wmma.cu:16-97): both products share the x tile and the epilogue is fused.
+//
+// Forward (tcgen05): a persistent CTA keeps both weight matrices in shared memory (loaded once)
+// and streams 128-row tiles of x through TMA.  Per 128-column chunk the MMA warp computes
+// p = x wp and g = x wg into tensor memory (double-buffered, so the epilogue of one chunk
+// overlaps the MMAs of the next); the biases enter as one extra K=16 MMA step, ones[128 x 16]
+// times a bias row, so the epilogue only evaluates mask * p * sigmoid(g) and stores.
+//
+// Backward (tcgen05, two kernels, both recompute p and g from x):
+//   gdp_bwd_dx: dp = dout*mask*s, dg = dout*mask*p*s*(1-s) into shared memory, then
+//               dx += dp wp^T + dg wg^T over the column chunks in tensor memory.
+//   gdp_bwd_dw: per 64-column chunk (a group of CTAs per chunk), dp and dg split into
+//               bf16 hi + lo parts so that dwp = x^T dp, dwg = x^T dg and the bias gradients
+//               (ones^T dp, ones^T dg) keep f32 accuracy; per-CTA sums are added at the end.
+//
+// Shapes outside the fast paths (K not a multiple of 16 or above 128, weights larger than the
+// shared-memory budget, unaligned pointers) take plain CUDA-core kernels.
+#include "attention_common.cuh"
+#include "host.h"
+
+namespace cfk {
+namespace gdp {
+namespace {
+
+constexpr int kThreads = 320; // 2 epilogue warpgroups + producer warp + MMA warp
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kMaxK = 128;
+constexpr int kWeightBudget = 128 * 1024; // both weight matrices, resident
+
+__device__ __forceinline__ float sigmoid_fast(float x) {
+    // sigmoid(x) = 0.5 * tanh(x / 2) + 0.5
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+    return fmaf(0.5f, t, 0.5f);
+}
+
+// sigmoid through exp2: f32-accurate (used by the backward, whose f32 outputs need it).
+__device__ __forceinline__ float sigmoid_accurate(float x) {
+    return 1.0f / (1.0f + ex2(-x * kLog2e));
+}
+
+// Offsets of the forward kernel's shared memory (bytes from a 1024-aligned base).
+struct FwdLayout {
+    int kb;        // K (multiple of 16, <= 128)
+    int npad;      // N rounded up to 128
+    int x_stage;   // one x tile: ceil(K/64) panels of 128 rows x 128 B
+    int off_x, off_wp, off_wg, off_bp, off_bg, off_ones, off_bar, total;
+};
+
+__host__ __device__ inline FwdLayout fwd_layout(int K, int N) {
+    FwdLayout L;
+    L.kb = K;
+    L.npad = (N + 127) / 128 * 128;
+    L.x_stage = ((K + 63) / 64) * 16384;
+    L.off_x = 0;
+    L.off_wp = 2 * L.x_stage;
+    L.off_wg = L.off_wp + L.kb * L.npad * 2;
+    L.off_bp = L.off_wg + L.kb * L.npad * 2;
+    L.off_bg = L.off_bp + (L.npad / 8) * 256;
+    L.off_ones = L.off_bg + (L.npad / 8) * 256;
+    L.off_bar = L.off_ones + 4096;
+    L.total = L.off_bar + 16 * 8 + 16 + 1024;
+    return L;
+}
+
+// Shared-memory descriptors (see attention_common.cuh for the layouts).
+// x tile, K-major, k-step s: panel s/4 of 64 columns, 32 B per 16 columns.
+__device__ __forceinline__ uint64_t x_desc(uint32_t x, int s) {
+    return smem_desc(x + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024, kSwizzle128);
+}
+// weight [K rows x n] stored as 64-column atoms of kb rows x 128 B, MN-major, columns
+// [128c, 128c + 128), k-step s.
+__device__ __forceinline__ uint64_t w_desc(uint32_t w, int kb, int c, int s) {
+    return smem_desc(w + 2 * c * (kb * 128) + s * 2048, kb * 128, 1024, kSwizzle128);
+}
+// bias row operand [16 x npad] (row 0 = bias), MN-major interleave: (kk, n) at
+// (n/8)*256 + kk*16 + (n%8)*2; columns [128c, 128c + 128).
+__device__ __forceinline__ uint64_t brow_desc(uint32_t b, int c) {
+    return smem_desc(b + c * 16 * 256, 128, 256, kInterleave);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    gdp_fwd_kernel(const __grid_constant__ CUtensorMap tm_x,
+                   const __grid_constant__ CUtensorMap tm_wp,
+                   const __grid_constant__ CUtensorMap tm_wg, const uint16_t* __restrict__ bp,
+                   const uint16_t* __restrict__ bg, const uint16_t* __restrict__ mask,
+                   uint16_t* __restrict__ out, int M, int K, int N) {
+    using E = Elem<T>;
+    const FwdLayout L = fwd_layout(K, N);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t sbase = smem_u32(smem);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.off_bar);
+    uint64_t* x_full = bars;        // [2]
+    uint64_t* x_empty = bars + 2;   // [2]
+    uint64_t* w_full = bars + 4;
+    uint64_t* acc_full = bars + 5;  // [2]
+    uint64_t* acc_empty = bars + 7; // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.off_bar + 16 * 8);
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n_mt = (M + 127) / 128;
+    const int n_chunks = L.npad / 128;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&x_full[i], 1);
+            mbar_init(&x_empty[i], 1);
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 8);
+        }
+        mbar_init(w_full, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    // bias rows (row 0 = bias, rows 1..15 = 0) and ones[128 x 16] (column 0 = 1), in T
+    {
+        uint16_t* sbp = reinterpret_cast<uint16_t*>(smem + L.off_bp);
+        uint16_t* sbg = reinterpret_cast<uint16_t*>(smem + L.off_bg);
+        const int nel = (L.npad / 8) * 128; // 16-bit elements per bias operand
+        for (int i = threadIdx.x; i < nel; i += blockDim.x) {
+            const int chunk = i / 128, within = i % 128, kk = within / 8, e = within % 8;
+            const int n = chunk * 8 + e;
+            const bool on = (kk == 0 && n < N);
+            sbp[i] = on ? bp[n] : uint16_t(0);
+            sbg[i] = on ? bg[n] : uint16_t(0);
+        }
+        const uint32_t one = E::kBf16 ? 0x3F80u : 0x3C00u;
+        uint32_t* ones = reinterpret_cast<uint32_t*>(smem + L.off_ones);
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+            ones[i] = ((i < 512) && ((i & 3) == 0)) ? one : 0u;
+        }
+        fence_proxy_async_smem();
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(tmem_slot, 512);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int n_mine = (n_mt - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                       static_cast<int>(gridDim.x);
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            // weights once: 64-column atoms of all K rows
+            const int atoms = L.npad / 64;
+            mbar_arrive_expect_tx(w_full, 2 * atoms * L.kb * 128);
+            for (int a = 0; a < atoms; ++a) {
+                tma_load_3d(smem + L.off_wp + a * L.kb * 128, &tm_wp, w_full, a * 64, 0, 0);
+                tma_load_3d(smem + L.off_wg + a * L.kb * 128, &tm_wg, w_full, a * 64, 0, 0);
+            }
+            const int panels = (K + 63) / 64;
+            for (int i = 0; i < n_mine; ++i) {
+                const int mt = blockIdx.x + i * gridDim.x;
+                const int s = i & 1;
+                if (i >= 2 && !mbar_wait(&x_empty[s], ((i >> 1) - 1) & 1, abort_flag)) {
+                    goto done;
+                }
+                mbar_arrive_expect_tx(&x_full[s], panels * 16384);
+                for (int pn = 0; pn < panels; ++pn) {
+                    tma_load_3d(smem + L.off_x + s * L.x_stage + pn * 16384, &tm_x, &x_full[s],
+                                pn * 64, mt * 128, 0);
+                }
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            constexpr uint32_t kId = idesc_f16(128, 128, false, true, E::kBf16);
+            constexpr uint32_t kIdBias = idesc_f16(128, 128, false, true, E::kBf16);
+            const uint64_t ones = attn::interleave16_kmajor(sbase + L.off_ones);
+            const int ksteps = K / 16;
+            if (!mbar_wait(w_full, 0, abort_flag)) {
+                goto done;
+            }
+            uint32_t chunk_ctr = 0;
+            for (int i = 0; i < n_mine; ++i) {
+                const int s = i & 1;
+                if (!mbar_wait(&x_full[s], (i >> 1) & 1, abort_flag)) {
+                    goto done;
+                }
+                tc_fence_after();
+                const uint32_t x = sbase + L.off_x + s * L.x_stage;
+                for (int c = 0; c < n_chunks; ++c, ++chunk_ctr) {
+                    const int bf = chunk_ctr & 1;
+                    if (chunk_ctr >= 2 &&
+                        !mbar_wait(&acc_empty[bf], ((chunk_ctr >> 1) - 1) & 1, abort_flag)) {
+                        goto done;
+                    }
+                    tc_fence_after();
+                    const uint32_t accp = tmem + bf * 256;
+                    const uint32_t accg = accp + 128;
+                    for (int ks = 0; ks < ksteps; ++ks) {
+                        umma_ss(accp, x_desc(x, ks), w_desc(sbase + L.off_wp, L.kb, c, ks), kId,
+                                ks > 0);
+                    }
+                    umma_ss(accp, ones, brow_desc(sbase + L.off_bp, c), kIdBias, 1);
+                    for (int ks = 0; ks < ksteps; ++ks) {
+                        umma_ss(accg, x_desc(x, ks), w_desc(sbase + L.off_wg, L.kb, c, ks), kId,
+                                ks > 0);
+                    }
+                    umma_ss(accg, ones, brow_desc(sbase + L.off_bg, c), kIdBias, 1);
+                    umma_commit(&acc_full[bf]);
+                }
+                umma_commit(&x_empty[s]);
+            }
+        }
+    } else {
+        // epilogue: thread (w, r) owns row r and columns [64w, 64w + 64) of each chunk
+        const int w = warp >> 2;
+        const int r = static_cast<int>(attn::warp_lane_base()) + lane;
+        const uint32_t lane_off = attn::warp_lane_base() << 16;
+        uint32_t chunk_ctr = 0;
+        for (int i = 0; i < n_mine; ++i) {
+            const int mt = blockIdx.x + i * gridDim.x;
+            const int row = mt * 128 + r;
+            const bool row_ok = row < M;
+            const float hm = row_ok ? 0.5f * E::to_float(mask[row]) : 0.f;
+            for (int c = 0; c < n_chunks; ++c, ++chunk_ctr) {
+                const int bf = chunk_ctr & 1;
+                if (!mbar_wait(&acc_full[bf], (chunk_ctr >> 1) & 1, abort_flag)) {
+                    goto done;
+                }
+                __syncwarp();
+                tc_fence_after();
+                const uint32_t accp = tmem + lane_off + bf * 256 + 64 * w;
+                const uint32_t accg = accp + 128;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t pv[16], gv[16];
+                    tmem_ld16(accp + 16 * q, pv);
+                    tmem_ld16(accg + 16 * q, gv);
+                    tmem_ld_wait();
+                    uint32_t o[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        float y[2];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const float p = __uint_as_float(pv[2 * e + h]);
+                            const float g = __uint_as_float(gv[2 * e + h]);
+                            float t;
+                            asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * g));
+                            y[h] = p * fmaf(hm, t, hm); // mask * p * (0.5 tanh(g/2) + 0.5)
+                        }
+                        o[e] = E::pack(y[0], y[1]);
+                    }
+                    const int n0 = c * 128 + 64 * w + 16 * q;
+                    if (row_ok && n0 < N) {
+                        uint16_t* dst = out + static_cast<int64_t>(row) * N + n0;
+                        st_global_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
+                        if (n0 + 8 < N) {
+                            st_global_v4(dst + 8, make_uint4(o[4], o[5], o[6], o[7]));
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&acc_empty[bf]);
+                }
+            }
+        }
+    }
+done:
+    __syncwarp();
+    if (*abort_flag) {
+        const unsigned long long t0 = global_ns();
+        while (global_ns() - t0 < 200000ull) {
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarp) {
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// CUDA-core kernels for shapes outside the tcgen05 paths.  16 x 16 output tiles, K in steps
+// of 16 through shared memory, f32 accumulation.
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void gdp_fwd_generic_kernel(const uint16_t* __restrict__ x,
+                                       const uint16_t* __restrict__ wp,
+                                       const uint16_t* __restrict__ bp,
+                                       const uint16_t* __restrict__ wg,
+                                       const uint16_t* __restrict__ bg,
+                                       const uint16_t* __restrict__ mask,
+                                       uint16_t* __restrict__ out, int M, int K, int N) {
+    using E = Elem<T>;
+    __shared__ float xs[16][17], ps[16][17], gs[16][17];
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    const int m = blockIdx.y * 16 + ty, n = blockIdx.x * 16 + tx;
+    float ap = 0.f, ag = 0.f;
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        const int mx = blockIdx.y * 16 + ty, kx = k0 + tx;
+        xs[ty][tx] = (mx < M && kx < K) ? E::to_float(x[static_cast<int64_t>(mx) * K + kx]) : 0.f;
+        const int kw = k0 + ty;
+        ps[ty][tx] = (kw < K && n < N) ? E::to_float(wp[static_cast<int64_t>(kw) * N + n]) : 0.f;
+        gs[ty][tx] = (kw < K && n < N) ? E::to_float(wg[static_cast<int64_t>(kw) * N + n]) : 0.f;
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+            ap = fmaf(xs[ty][kk], ps[kk][tx], ap);
+            ag = fmaf(xs[ty][kk], gs[kk][tx], ag);
+        }
+        __syncthreads();
+    }
+    if (m < M && n < N) {
+        const float p = ap + E::to_float(bp[n]);
+        const float g = ag + E::to_float(bg[n]);
+        out[static_cast<int64_t>(m) * N + n] = E::from_float(E::to_float(mask[m]) * p * sigmoid_accurate(g));
+    }
+}
+
+template <typename T>
+int gdp_fwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const void* wp,
+                 const void* bp, const void* wg, const void* bg, const void* mask, void* out,
+                 int M, int K, int N) {
+    const FwdLayout L = fwd_layout(K, N);
+    const bool fast = (K % 16 == 0) && K >= 16 && K <= kMaxK &&
+                      2 * L.kb * L.npad * 2 <= kWeightBudget && aligned16(x) && aligned16(wp) &&
+                      aligned16(wg) && aligned16(out) && L.total <= 227 * 1024;
+    if (!fast) {
+        dim3 block(16, 16), grid((N + 15) / 16, (M + 15) / 16);
+        gdp_fwd_generic_kernel<T><<<grid, block, 0, st>>>(
+            static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(wp),
+            static_cast<const uint16_t*>(bp), static_cast<const uint16_t*>(wg),
+            static_cast<const uint16_t*>(bg), static_cast<const uint16_t*>(mask),
+            static_cast<uint16_t*>(out), M, K, N);
+        return check_launch("gdp_fwd_generic");
+    }
+    CUtensorMap tx, twp, twg;
+    // x [M, K]: dims (K, M, 1), box 64 x 128; weights [K, N]: dims (N, K, 1), box 64 x K
+    CFK_TRY(make_tmap_3d(&tx, x, K, M, 1, 2ull * K, 2ull * K * M, 64, 128, 1, 128, "gdp x"));
+    CFK_TRY(make_tmap_3d(&twp, wp, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wp"));
+    CFK_TRY(make_tmap_3d(&twg, wg, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wg"));
+    auto kern = gdp_fwd_kernel<T>;
+    CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
+                             "gdp_fwd"));
+    const int n_mt = (M + 127) / 128;
+    const int grid = std::min(n_mt, dev.num_sms);
+    kern<<<grid, kThreads, L.total, st>>>(tx, twp, twg, static_cast<const uint16_t*>(bp),
+                                          static_cast<const uint16_t*>(bg),
+                                          static_cast<const uint16_t*>(mask),
+                                          static_cast<uint16_t*>(out), M, K, N);
+    return check_launch("gdp_fwd");
+}
+
+// ==========================================================================================
+// Backward
+// ==========================================================================================
+// dp = dout * mask * s and dg = dout * mask * p * s * (1 - s), s = sigmoid(g), in f32.
+__device__ __forceinline__ void gate_grads(float p, float g, float dout, float m, float& dp,
+                                           float& dg) {
+    const float s = sigmoid_accurate(g);
+    const float dm = dout * m;
+    dp = dm * s;
+    dg = dm * p * s * (1.f - s);
+}
+
+// bias-row operand of one 128- or 64-column chunk, built in shared memory by one warp:
+// MN-major interleave [16 x cols], row 0 = bias[n0 + n] (0 beyond N), rows 1..15 = 0.
+__device__ __forceinline__ void build_brow(uint16_t* dst, const uint16_t* bias, int n0, int cols,
+                                           int N, int lane) {
+    for (int i = lane; i < cols * 16; i += 32) {
+        const int chunk = i / 128, within = i % 128, kk = within / 8, e = within % 8;
+        const int n = n0 + chunk * 8 + e;
+        dst[i] = (kk == 0 && n < N) ? bias[n] : uint16_t(0);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// dx = dp wp^T + dg wg^T, per 128-row tile of x; p and g recomputed per 128-column chunk.
+// ------------------------------------------------------------------------------------------
+struct DxLayout {
+    int x, wp, wg, dout, dp, dg, bp, bg, ones, bar, total;
+};
+
+__host__ __device__ inline DxLayout dx_layout(int K) {
+    DxLayout L;
+    const int wchunk = K * 256; // [K rows x 128 n] = 2 atoms of K x 128 B
+    L.x = 0;                    // 2 panels (zero-filled beyond K)
+    L.wp = 32768;
+    L.wg = L.wp + wchunk;
+    L.dout = L.wg + wchunk;     // [128 x 128] 2 panels
+    L.dp = L.dout + 32768;
+    L.dg = L.dp + 32768;
+    L.bp = L.dg + 32768;        // [16 x 128] interleave, 4 KB
+    L.bg = L.bp + 4096;
+    L.ones = L.bg + 4096;
+    L.bar = L.ones + 4096;
+    L.total = L.bar + 16 * 8 + 16 + 1024;
+    return L;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    gdp_bwd_dx_kernel(const __grid_constant__ CUtensorMap tm_x,
+                      const __grid_constant__ CUtensorMap tm_wp,
+                      const __grid_constant__ CUtensorMap tm_wg,
+                      const __grid_constant__ CUtensorMap tm_dout,
+                      const uint16_t* __restrict__ bp, const uint16_t* __restrict__ bg,
+                      const uint16_t* __restrict__ mask, uint16_t* __restrict__ dx, int M, int K,
+                      int N) {
+    using E = Elem<T>;
+    const DxLayout L = dx_layout(K);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t sbase = smem_u32(smem);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar);
+    uint64_t* x_full = bars + 0;
+    uint64_t* tile_done = bars + 1;   // all MMAs of a row tile done (x free)
+    uint64_t* chunk_full = bars + 2;  // w chunk, dout chunk, bias rows loaded
+    uint64_t* rec_full = bars + 3;    // p, g of the chunk in tensor memory
+    uint64_t* ds_full = bars + 4;     // dp, dg written (count 8)
+    uint64_t* dx_done = bars + 5;     // dx MMAs of the chunk done (chunk buffers free)
+    uint64_t* dx_full = bars + 6;     // dx of the tile complete
+    uint64_t* dx_drained = bars + 7;  // dx read out of tensor memory (count 8)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + 16 * 8);
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n_mt = (M + 127) / 128;
+    const int n_chunks = (N + 127) / 128;
+    const int n_mine = (n_mt - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                       static_cast<int>(gridDim.x);
+
+    if (threadIdx.x == 0) {
+        mbar_init(x_full, 1);
+        mbar_init(tile_done, 1);
+        mbar_init(chunk_full, 1);
+        mbar_init(rec_full, 1);
+        mbar_init(ds_full, 8);
+        mbar_init(dx_done, 1);
+        mbar_init(dx_full, 1);
+        mbar_init(dx_drained, 8);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    {
+        const uint32_t one = E::kBf16 ? 0x3F80u : 0x3C00u;
+        uint32_t* ones = reinterpret_cast<uint32_t*>(smem + L.ones);
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+            ones[i] = ((i < 512) && ((i & 3) == 0)) ? one : 0u;
+        }
+        if (K <= 64) { // the second x panel stays zero
+            uint32_t* z = reinterpret_cast<uint32_t*>(smem + L.x + 16384);
+            for (int i = threadIdx.x; i < 4096; i += blockDim.x) {
+                z[i] = 0u;
+            }
+        }
+        fence_proxy_async_smem();
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(tmem_slot, 512);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // tensor memory: p at 0, g at 128, dx at 256 (K columns)
+
+    if (warp == kProducerWarp) {
+        uint32_t cc = 0; // chunk counter
+        for (int i = 0; i < n_mine; ++i) {
+            const int mt = blockIdx.x + i * gridDim.x;
+            if (i > 0 && !mbar_wait(tile_done, (i - 1) & 1, abort_flag)) {
+                goto done;
+            }
+            if (lane == 0) {
+                const int panels = (K + 63) / 64;
+                mbar_arrive_expect_tx(x_full, panels * 16384);
+                for (int pn = 0; pn < panels; ++pn) {
+                    tma_load_3d(smem + L.x + pn * 16384, &tm_x, x_full, pn * 64, mt * 128, 0);
+                }
+            }
+            for (int c = 0; c < n_chunks; ++c, ++cc) {
+                if (cc > 0 && !mbar_wait(dx_done, (cc - 1) & 1, abort_flag)) {
+                    goto done;
+                }
+                build_brow(reinterpret_cast<uint16_t*>(smem + L.bp), bp, c * 128, 128, N, lane);
+                build_brow(reinterpret_cast<uint16_t*>(smem + L.bg), bg, c * 128, 128, N, lane);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(chunk_full, 2 * 2 * K * 128 + 32768);
+                    for (int a = 0; a < 2; ++a) {
+                        tma_load_3d(smem + L.wp + a * K * 128, &tm_wp, chunk_full,
+                                    c * 128 + a * 64, 0, 0);
+                        tma_load_3d(smem + L.wg + a * K * 128, &tm_wg, chunk_full,
+                                    c * 128 + a * 64, 0, 0);
+                        tma_load_3d(smem + L.dout + a * 16384, &tm_dout, chunk_full,
+                                    c * 128 + a * 64, mt * 128, 0);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            constexpr uint32_t kIdRec = idesc_f16(128, 128, false, true, E::kBf16);
+            const uint32_t kIdDx = idesc_f16(128, K, false, false, E::kBf16);
+            const uint64_t ones = attn::interleave16_kmajor(sbase + L.ones);
+            const int ksteps = K / 16;
+            uint32_t cc = 0;
+            for (int i = 0; i < n_mine; ++i) {
+                if (!mbar_wait(x_full, i & 1, abort_flag)) {
+                    goto done;
+                }
+                for (int c = 0; c < n_chunks; ++c, ++cc) {
+                    if (!mbar_wait(chunk_full, cc & 1, abort_flag)) {
+                        goto done;
+                    }
+                    tc_fence_after();
+                    for (int ks = 0; ks < ksteps; ++ks) {
+                        umma_ss(tmem, x_desc(sbase + L.x, ks), w_desc(sbase + L.wp, K, 0, ks),
+                                kIdRec, ks > 0);
+                    }
+                    umma_ss(tmem, ones, brow_desc(sbase + L.bp, 0), kIdRec, 1);
+                    for (int ks = 0; ks < ksteps; ++ks) {
+                        umma_ss(tmem + 128, x_desc(sbase + L.x, ks),
+                                w_desc(sbase + L.wg, K, 0, ks), kIdRec, ks > 0);
+                    }
+                    umma_ss(tmem + 128, ones, brow_desc(sbase + L.bg, 0), kIdRec, 1);
+                    umma_commit(rec_full);
+                    if (!mbar_wait(ds_full, cc & 1, abort_flag)) {
+                        goto done;
+                    }
+                    if (c == 0 && i > 0 && !mbar_wait(dx_drained, (i - 1) & 1, abort_flag)) {
+                        goto done;
+                    }
+                    tc_fence_after();
+                    // dx[m, k] += sum_n dp[m, n] wp[k, n]: A = dp K-major, B = w chunk K-major
+#pragma unroll
+                    for (int ks = 0; ks < 8; ++ks) {
+                        const uint32_t boff = (ks >> 2) * (K * 128) + (ks & 3) * 32;
+                        umma_ss(tmem + 256, x_desc(sbase + L.dp, ks),
+                                smem_desc(sbase + L.wp + boff, 16, 1024, kSwizzle128), kIdDx,
+                                (c > 0 || ks > 0) ? 1u : 0u);
+                        umma_ss(tmem + 256, x_desc(sbase + L.dg, ks),
+                                smem_desc(sbase + L.wg + boff, 16, 1024, kSwizzle128), kIdDx, 1);
+                    }
+                    umma_commit(dx_done);
+                }
+                umma_commit(tile_done);
+                umma_commit(dx_full);
+            }
+        }
+    } else {
+        const int w = warp >> 2;
+        const int r = static_cast<int>(attn::warp_lane_base()) + lane;
+        const uint32_t lane_off = attn::warp_lane_base() << 16;
+        const uint32_t dp_row = sbase + L.dp + w * 16384 + r * 128;
+        const uint32_t dg_row = sbase + L.dg + w * 16384 + r * 128;
+        const uint32_t do_row = sbase + L.dout + w * 16384 + r * 128;
+        uint32_t cc = 0;
+        for (int i = 0; i < n_mine; ++i) {
+            const int mt = blockIdx.x + i * gridDim.x;
+            const int row = mt * 128 + r;
+            const bool row_ok = row < M;
+            const float mk = row_ok ? E::to_float(mask[row]) : 0.f;
+            for (int c = 0; c < n_chunks; ++c, ++cc) {
+                if (!mbar_wait(rec_full, cc & 1, abort_flag) ||
+                    !mbar_wait(chunk_full, cc & 1, abort_flag)) {
+                    goto done;
+                }
+                // dp / dg shared buffers are free once the previous chunk's dx MMAs are done
+                if (cc > 0 && !mbar_wait(dx_done, (cc - 1) & 1, abort_flag)) {
+                    goto done;
+                }
+                __syncwarp();
+                tc_fence_after();
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t pv[16], gv[16];
+                    tmem_ld16(tmem + lane_off + 64 * w + 16 * q, pv);
+                    tmem_ld16(tmem + lane_off + 128 + 64 * w + 16 * q, gv);
+                    tmem_ld_wait();
+                    uint32_t op[8], og[8];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint4 dw = attn::lds128(do_row + (((2 * q + h) ^ (r & 7)) << 4));
+                        const uint32_t dww[4] = {dw.x, dw.y, dw.z, dw.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 d2 = E::to_float2(dww[e]);
+                            float dp0, dg0, dp1, dg1;
+                            gate_grads(__uint_as_float(pv[8 * h + 2 * e]),
+                                       __uint_as_float(gv[8 * h + 2 * e]), d2.x, mk, dp0, dg0);
+                            gate_grads(__uint_as_float(pv[8 * h + 2 * e + 1]),
+                                       __uint_as_float(gv[8 * h + 2 * e + 1]), d2.y, mk, dp1, dg1);
+                            op[4 * h + e] = E::pack(dp0, dp1);
+                            og[4 * h + e] = E::pack(dg0, dg1);
+                        }
+                    }
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t off = ((2 * q + h) ^ (r & 7)) << 4;
+                        attn::sts128(dp_row + off, make_uint4(op[4 * h], op[4 * h + 1], op[4 * h + 2], op[4 * h + 3]));
+                        attn::sts128(dg_row + off, make_uint4(og[4 * h], og[4 * h + 1], og[4 * h + 2], og[4 * h + 3]));
+                    }
+                }
+                tc_fence_before();
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(ds_full);
+                }
+            }
+            // dx of the tile: thread (w, r) stores columns [w*K/2, (w+1)*K/2)
+            if (!mbar_wait(dx_full, i & 1, abort_flag)) {
+                goto done;
+            }
+            __syncwarp();
+            tc_fence_after();
+            const int half = K / 2;
+            for (int q = 0; q < half; q += 8) {
+                uint32_t v[8];
+                tmem_ld8(tmem + lane_off + 256 + w * half + q, v);
+                tmem_ld_wait();
+                if (row_ok) {
+                    uint4 o = make_uint4(E::pack(__uint_as_float(v[0]), __uint_as_float(v[1])),
+                                         E::pack(__uint_as_float(v[2]), __uint_as_float(v[3])),
+                                         E::pack(__uint_as_float(v[4]), __uint_as_float(v[5])),
+                                         E::pack(__uint_as_float(v[6]), __uint_as_float(v[7])));
+                    st_global_v4(dx + static_cast<int64_t>(row) * K + w * half + q, o);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(dx_drained);
+            }
+        }
+    }
+done:
+    __syncwarp();
+    if (*abort_flag) {
+        const unsigned long long t0 = global_ns();
+        while (global_ns() - t0 < 200000ull) {
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarp) {
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// dwp, dwg, dbp, dbg for one 64-column chunk per CTA (a group of CTAs per chunk, each over a
+// strided set of row tiles); per-CTA sums are added into the zeroed f32 outputs at the end.
+// ------------------------------------------------------------------------------------------
+struct DwLayout {
+    int x, dout, hi_p, lo_p, hi_g, lo_g, wp, wg, bp, bg, ones, red, bar, total;
+};
+
+__host__ __device__ inline DwLayout dw_layout(int K) {
+    DwLayout L;
+    L.x = 0;                  // 2 stages x 2 panels x 16 KB
+    L.dout = 65536;           // 2 stages x [128 x 64] (one 16 KB panel)
+    L.hi_p = L.dout + 32768;  // four [128 x 64] bf16 tiles
+    L.lo_p = L.hi_p + 16384;
+    L.hi_g = L.lo_p + 16384;
+    L.lo_g = L.hi_g + 16384;
+    L.wp = L.lo_g + 16384;    // [K rows x 64 n] = K x 128 B
+    L.wg = L.wp + K * 128;
+    L.bp = L.wg + K * 128;    // [16 x 64] interleave, 2 KB
+    L.bg = L.bp + 2048;
+    L.ones = L.bg + 2048;
+    L.red = L.ones + 4096;    // f32 [8 warps][64] bias-gradient partials
+    L.bar = L.red + 8 * 64 * 4;
+    L.total = L.bar + 16 * 8 + 16 + 1024;
+    return L;
+}
+
+// Column sums of v[0..31] over the 32 lanes: afterwards lane l holds the sum of column l.
+__device__ __forceinline__ float warp_column_sum32(float (&v)[32], int lane) {
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        const bool up = (lane & s) != 0;
+#pragma unroll
+        for (int i = 0; i < s; ++i) {
+            const float send = up ? v[i] : v[i + s];
+            const float keep = up ? v[i + s] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+        }
+    }
+    return v[0];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    gdp_bwd_dw_kernel(const __grid_constant__ CUtensorMap tm_x,
+                      const __grid_constant__ CUtensorMap tm_wp,
+                      const __grid_constant__ CUtensorMap tm_wg,
+                      const __grid_constant__ CUtensorMap tm_dout,
+                      const uint16_t* __restrict__ bp, const uint16_t* __restrict__ bg,
+                      const uint16_t* __restrict__ mask, float* __restrict__ dwp,
+                      float* __restrict__ dwg, float* __restrict__ dbp, float* __restrict__ dbg,
+                      int M, int K, int N, int n_groups) {
+    using E = Elem<T>;
+    const DwLayout L = dw_layout(K);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t sbase = smem_u32(smem);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar);
+    uint64_t* w_full = bars + 0;
+    uint64_t* in_full = bars + 1;    // [2] x tile + dout chunk
+    uint64_t* in_empty = bars + 3;   // [2]
+    uint64_t* rec_full = bars + 5;
+    uint64_t* ds_full = bars + 6;    // count 8
+    uint64_t* dw_done = bars + 7;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + 16 * 8);
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(tmem_slot + 1);
+    float* red = reinterpret_cast<float*>(smem + L.red);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n_mt = (M + 127) / 128;
+    const int chunk = blockIdx.x % ((N + 63) / 64);
+    const int group = blockIdx.x / ((N + 63) / 64);
+    const int n0 = chunk * 64;
+    const int n_mine = (n_mt - group + n_groups - 1) / n_groups;
+
+    if (threadIdx.x == 0) {
+        mbar_init(w_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&in_full[s], 1);
+            mbar_init(&in_empty[s], 1);
+        }
+        mbar_init(rec_full, 1);
+        mbar_init(ds_full, 8);
+        mbar_init(dw_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    {
+        const uint32_t one = E::kBf16 ? 0x3F80u : 0x3C00u;
+        uint32_t* ones = reinterpret_cast<uint32_t*>(smem + L.ones);
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+            ones[i] = ((i < 512) && ((i & 3) == 0)) ? one : 0u;
+        }
+        if (K <= 64) {
+            for (int s = 0; s < 2; ++s) {
+                uint32_t* z = reinterpret_cast<uint32_t*>(smem + L.x + s * 32768 + 16384);
+                for (int i = threadIdx.x; i < 4096; i += blockDim.x) {
+                    z[i] = 0u;
+                }
+            }
+        }
+        for (int i = threadIdx.x; i < 8 * 64; i += blockDim.x) {
+            red[i] = 0.f;
+        }
+        if (warp == 0) {
+            build_brow(reinterpret_cast<uint16_t*>(smem + L.bp), bp, n0, 64, N, lane);
+            build_brow(reinterpret_cast<uint16_t*>(smem + L.bg), bg, n0, 64, N, lane);
+        }
+        fence_proxy_async_smem();
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(tmem_slot, 256);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // tensor memory: p at 0, g at 64, dwp at 128, dwg at 192
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(w_full, 2 * K * 128);
+            tma_load_3d(smem + L.wp, &tm_wp, w_full, n0, 0, 0);
+            tma_load_3d(smem + L.wg, &tm_wg, w_full, n0, 0, 0);
+            const int panels = (K + 63) / 64;
+            for (int i = 0; i < n_mine; ++i) {
+                const int mt = group + i * n_groups;
+                const int s = i & 1;
+                if (i >= 2 && !mbar_wait(&in_empty[s], ((i >> 1) - 1) & 1, abort_flag)) {
+                    goto done;
+                }
+                mbar_arrive_expect_tx(&in_full[s], panels * 16384 + 16384);
+                for (int pn = 0; pn < panels; ++pn) {
+                    tma_load_3d(smem + L.x + s * 32768 + pn * 16384, &tm_x, &in_full[s],
+                                pn * 64, mt * 128, 0);
+                }
+                tma_load_3d(smem + L.dout + s * 16384, &tm_dout, &in_full[s], n0, mt * 128, 0);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            constexpr uint32_t kIdRec = idesc_f16(128, 64, false, true, E::kBf16);
+            constexpr uint32_t kIdDw = idesc_f16(128, 64, true, true, E::kBf16);
+            const uint64_t ones = attn::interleave16_kmajor(sbase + L.ones);
+            const int ksteps = K / 16;
+            if (!mbar_wait(w_full, 0, abort_flag)) {
+                goto done;
+            }
+            auto issue_dw = [&](int i) {
+                // dw[k, n] += sum_m x[m, k] (hi + lo)[m, n]: A = x^T (MN-major), B MN-major
+                const uint32_t xs = sbase + L.x + (i & 1) * 32768;
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint64_t a = smem_desc(xs + ks * 2048, 16384, 1024, kSwizzle128);
+                    const uint32_t acc = (i > 0 || ks > 0) ? 1u : 0u;
+                    umma_ss(tmem + 128, a, smem_desc(sbase + L.hi_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
+                    umma_ss(tmem + 128, a, smem_desc(sbase + L.lo_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
+                    umma_ss(tmem + 192, a, smem_desc(sbase + L.hi_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
+                    umma_ss(tmem + 192, a, smem_desc(sbase + L.lo_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
+                }
+                umma_commit(dw_done);
+                umma_commit(&in_empty[i & 1]);
+            };
+            for (int i = 0; i < n_mine; ++i) {
+                const int s = i & 1;
+                if (!mbar_wait(&in_full[s], (i >> 1) & 1, abort_flag)) {
+                    goto done;
+                }
+                if (i > 0) {
+                    // tensor memory p, g is free once the epilogue has read tile i-1
+                    if (!mbar_wait(ds_full, (i - 1) & 1, abort_flag)) {
+                        goto done;
+                    }
+                    tc_fence_after();
+                    issue_dw(i - 1);
+                }
+                const uint32_t xs = sbase + L.x + s * 32768;
+                for (int ks = 0; ks < ksteps; ++ks) {
+                    umma_ss(tmem, x_desc(xs, ks), smem_desc(sbase + L.wp + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
+                }
+                umma_ss(tmem, ones, smem_desc(sbase + L.bp, 128, 256, kInterleave), kIdRec, 1);
+                for (int ks = 0; ks < ksteps; ++ks) {
+                    umma_ss(tmem + 64, x_desc(xs, ks), smem_desc(sbase + L.wg + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
+                }
+                umma_ss(tmem + 64, ones, smem_desc(sbase + L.bg, 128, 256, kInterleave), kIdRec, 1);
+                umma_commit(rec_full);
+            }
+            if (n_mine > 0) {
+                if (!mbar_wait(ds_full, (n_mine - 1) & 1, abort_flag)) {
+                    goto done;
+                }
+                tc_fence_after();
+                issue_dw(n_mine - 1);
+            }
+        }
+    } else {
+        const int w = warp >> 2;
+        const int r = static_cast<int>(attn::warp_lane_base()) + lane;
+        const uint32_t lane_off = attn::warp_lane_base() << 16;
+        float colsum_p = 0.f, colsum_g = 0.f; // this lane's column of the warp's 32 columns
+        for (int i = 0; i < n_mine; ++i) {
+            const int mt = group + i * n_groups;
+            const int row = mt * 128 + r;
+            const bool row_ok = row < M;
+            const float mk = row_ok ? E::to_float(mask[row]) : 0.f;
+            if (!mbar_wait(rec_full, i & 1, abort_flag) ||
+                !mbar_wait(&in_full[i & 1], (i >> 1) & 1, abort_flag)) {
+                goto done;
+            }
+            // hi / lo tiles are free once the dw MMAs of tile i-1 are done
+            if (i > 0 && !mbar_wait(dw_done, (i - 1) & 1, abort_flag)) {
+                goto done;
+            }
+            __syncwarp();
+            tc_fence_after();
+            float vp[32], vg[32];
+            {
+                uint32_t pv[32], gv[32];
+                tmem_ld32(tmem + lane_off + 32 * w, pv);
+                tmem_ld32(tmem + lane_off + 64 + 32 * w, gv);
+                tmem_ld_wait();
+                const uint32_t do_row = sbase + L.dout + (i & 1) * 16384 + r * 128;
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const uint4 dw4 = attn::lds128(do_row + (((4 * w + h) ^ (r & 7)) << 4));
+                    const uint32_t dww[4] = {dw4.x, dw4.y, dw4.z, dw4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 d2 = E::to_float2(dww[e]);
+                        const int j = 8 * h + 2 * e;
+                        gate_grads(__uint_as_float(pv[j]), __uint_as_float(gv[j]), d2.x, mk,
+                                   vp[j], vg[j]);
+                        gate_grads(__uint_as_float(pv[j + 1]), __uint_as_float(gv[j + 1]), d2.y,
+                                   mk, vp[j + 1], vg[j + 1]);
+                    }
+                }
+            }
+            // hi + lo split (16-bit each) into the four MMA operand tiles
+            const uint32_t rowoff = r * 128;
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                uint32_t hp[4], lp[4], hg[4], lg[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 8 * h + 2 * e;
+                    hp[e] = E::pack(vp[j], vp[j + 1]);
+                    hg[e] = E::pack(vg[j], vg[j + 1]);
+                    const float2 bpf = E::to_float2(hp[e]);
+                    const float2 bgf = E::to_float2(hg[e]);
+                    lp[e] = E::pack(vp[j] - bpf.x, vp[j + 1] - bpf.y);
+                    lg[e] = E::pack(vg[j] - bgf.x, vg[j + 1] - bgf.y);
+                }
+                const uint32_t off = rowoff + (((4 * w + h) ^ (r & 7)) << 4);
+                attn::sts128(sbase + L.hi_p + off, make_uint4(hp[0], hp[1], hp[2], hp[3]));
+                attn::sts128(sbase + L.lo_p + off, make_uint4(lp[0], lp[1], lp[2], lp[3]));
+                attn::sts128(sbase + L.hi_g + off, make_uint4(hg[0], hg[1], hg[2], hg[3]));
+                attn::sts128(sbase + L.lo_g + off, make_uint4(lg[0], lg[1], lg[2], lg[3]));
+            }
+            tc_fence_before();
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(ds_full);
+            }
+            // bias gradients: column sums over this warp's 32 rows
+            colsum_p += warp_column_sum32(vp, lane);
+            colsum_g += warp_column_sum32(vg, lane);
+        }
+        // combine the 4 row quarters of each warpgroup, then add into the outputs
+        red[warp * 64 + lane] = colsum_p;
+        red[warp * 64 + 32 + lane] = colsum_g;
+        named_bar_sync(1, 256);
+        if (threadIdx.x < 64) {
+            const int ww = threadIdx.x / 32, col = threadIdx.x % 32;
+            float sp = 0.f, sg = 0.f;
+            for (int q = 0; q < 4; ++q) {
+                sp += red[(4 * ww + q) * 64 + col];
+                sg += red[(4 * ww + q) * 64 + 32 + col];
+            }
+            const int n = n0 + 32 * ww + col;
+            if (n < N && n_mine > 0) {
+                atomicAdd(dbp + n, sp);
+                atomicAdd(dbg + n, sg);
+            }
+        }
+        // weight gradients: thread (w, r) owns row k = r, columns [32w, 32w + 32)
+        if (n_mine > 0) {
+            if (!mbar_wait(dw_done, (n_mine - 1) & 1, abort_flag)) {
+                goto done;
+            }
+            __syncwarp();
+            tc_fence_after();
+            uint32_t a[32], b[32];
+            tmem_ld32(tmem + lane_off + 128 + 32 * w, a);
+            tmem_ld32(tmem + lane_off + 192 + 32 * w, b);
+            tmem_ld_wait();
+            if (r < K) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int n = n0 + 32 * w + j;
+                    if (n < N) {
+                        atomicAdd(dwp + static_cast<int64_t>(r) * N + n, __uint_as_float(a[j]));
+                        atomicAdd(dwg + static_cast<int64_t>(r) * N + n, __uint_as_float(b[j]));
+                    }
+                }
+            }
+        }
+    }
+done:
+    __syncwarp();
+    if (*abort_flag) {
+        const unsigned long long t0 = global_ns();
+        while (global_ns() - t0 < 200000ull) {
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarp) {
+        tmem_dealloc(tmem, 256);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// CUDA-core backward for shapes outside the tcgen05 paths (workspace: f32 dp, dg [M, N]).
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void gdp_bwd_generic_grads_kernel(const uint16_t* __restrict__ x,
+                                             const uint16_t* __restrict__ wp,
+                                             const uint16_t* __restrict__ bp,
+                                             const uint16_t* __restrict__ wg,
+                                             const uint16_t* __restrict__ bg,
+                                             const uint16_t* __restrict__ mask,
+                                             const uint16_t* __restrict__ dout,
+                                             float* __restrict__ dpw, float* __restrict__ dgw,
+                                             int M, int K, int N) {
+    using E = Elem<T>;
+    __shared__ float xs[16][17], ps[16][17], gs[16][17];
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    const int m = blockIdx.y * 16 + ty, n = blockIdx.x * 16 + tx;
+    float ap = 0.f, ag = 0.f;
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        const int kx = k0 + tx, kw = k0 + ty;
+        xs[ty][tx] = (m < M && kx < K) ? E::to_float(x[static_cast<int64_t>(m) * K + kx]) : 0.f;
+        ps[ty][tx] = (kw < K && n < N) ? E::to_float(wp[static_cast<int64_t>(kw) * N + n]) : 0.f;
+        gs[ty][tx] = (kw < K && n < N) ? E::to_float(wg[static_cast<int64_t>(kw) * N + n]) : 0.f;
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+            ap = fmaf(xs[ty][kk], ps[kk][tx], ap);
+            ag = fmaf(xs[ty][kk], gs[kk][tx], ag);
+        }
+        __syncthreads();
+    }
+    if (m < M && n < N) {
+        float dp, dg;
+        gate_grads(ap + E::to_float(bp[n]), ag + E::to_float(bg[n]),
+                   E::to_float(dout[static_cast<int64_t>(m) * N + n]), E::to_float(mask[m]), dp,
+                   dg);
+        dpw[static_cast<int64_t>(m) * N + n] = dp;
+        dgw[static_cast<int64_t>(m) * N + n] = dg;
+    }
+}
+
+// dx[m, k] = sum_n dp[m, n] wp[k, n] + dg[m, n] wg[k, n]
+template <typename T>
+__global__ void gdp_bwd_generic_dx_kernel(const float* __restrict__ dpw,
+                                          const float* __restrict__ dgw,
+                                          const uint16_t* __restrict__ wp,
+                                          const uint16_t* __restrict__ wg,
+                                          uint16_t* __restrict__ dx, int M, int K, int N) {
+    using E = Elem<T>;
+    __shared__ float a[16][17], b[16][17], c[16][17], d[16][17];
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    const int m = blockIdx.y * 16 + ty, k = blockIdx.x * 16 + tx;
+    float acc = 0.f;
+    for (int n0 = 0; n0 < N; n0 += 16) {
+        const int na = n0 + tx;
+        a[ty][tx] = (m < M && na < N) ? dpw[static_cast<int64_t>(m) * N + na] : 0.f;
+        b[ty][tx] = (m < M && na < N) ? dgw[static_cast<int64_t>(m) * N + na] : 0.f;
+        const int kb = blockIdx.x * 16 + ty; // weight row for column tx of the n tile
+        c[ty][tx] = (kb < K && na < N) ? E::to_float(wp[static_cast<int64_t>(kb) * N + na]) : 0.f;
+        d[ty][tx] = (kb < K && na < N) ? E::to_float(wg[static_cast<int64_t>(kb) * N + na]) : 0.f;
+        __syncthreads();
+#pragma unroll
+        for (int nn = 0; nn < 16; ++nn) {
+            acc = fmaf(a[ty][nn], c[tx][nn], acc);
+            acc = fmaf(b[ty][nn], d[tx][nn], acc);
+        }
+        __syncthreads();
+    }
+    if (m < M && k < K) {
+        dx[static_cast<int64_t>(m) * K + k] = E::from_float(acc);
+    }
+}
+
+// dwp[k, n] = sum_m x[m, k] dp[m, n] (same for g); dbp[n] = sum_m dp[m, n]
+template <typename T>
+__global__ void gdp_bwd_generic_dw_kernel(const uint16_t* __restrict__ x,
+                                          const float* __restrict__ dpw,
+                                          const float* __restrict__ dgw, float* __restrict__ dwp,
+                                          float* __restrict__ dwg, float* __restrict__ dbp,
+                                          float* __restrict__ dbg, int M, int K, int N) {
+    using E = Elem<T>;
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int k = blockIdx.y; // k == K computes the bias gradients
+    if (n >= N) {
+        return;
+    }
+    float sp = 0.f, sg = 0.f;
+    for (int m = 0; m < M; ++m) {
+        const float xv = (k < K) ? E::to_float(x[static_cast<int64_t>(m) * K + k]) : 1.f;
+        sp = fmaf(xv, dpw[static_cast<int64_t>(m) * N + n], sp);
+        sg = fmaf(xv, dgw[static_cast<int64_t>(m) * N + n], sg);
+    }
+    if (k < K) {
+        dwp[static_cast<int64_t>(k) * N + n] = sp;
+        dwg[static_cast<int64_t>(k) * N + n] = sg;
+    } else {
+        dbp[n] = sp;
+        dbg[n] = sg;
+    }
+}
+
+bool bwd_fast_shape(int64_t K, int64_t N) {
+    return K % 16 == 0 && K >= 16 && K <= kMaxK && N % 8 == 0;
+}
+
+template <typename T>
+int gdp_bwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const void* wp,
+                 const void* bp, const void* wg, const void* bg, const void* mask,
+                 const void* dout, void* dx, float* dwp, float* dbp, float* dwg, float* dbg,
+                 void* ws, size_t ws_bytes, int M, int K, int N) {
+    const uint16_t* xs = static_cast<const uint16_t*>(x);
+    const uint16_t* wps = static_cast<const uint16_t*>(wp);
+    const uint16_t* wgs = static_cast<const uint16_t*>(wg);
+    const uint16_t* bps = static_cast<const uint16_t*>(bp);
+    const uint16_t* bgs = static_cast<const uint16_t*>(bg);
+    const uint16_t* ms = static_cast<const uint16_t*>(mask);
+    const uint16_t* dos = static_cast<const uint16_t*>(dout);
+    const bool fast = bwd_fast_shape(K, N) && aligned16(x) && aligned16(wp) && aligned16(wg) &&
+                      aligned16(dout) && aligned16(dx);
+    if (!fast) {
+        const size_t need = static_cast<size_t>(M) * N * 8;
+        if (!ws || ws_bytes < need) {
+            return fail(CFK_ERR_INVALID_ARGUMENT,
+                        "cfk_gdp_bwd: this shape or alignment needs a %zu-byte workspace", need);
+        }
+        float* dpw = static_cast<float*>(ws);
+        float* dgw = dpw + static_cast<size_t>(M) * N;
+        dim3 block(16, 16);
+        gdp_bwd_generic_grads_kernel<T><<<dim3((N + 15) / 16, (M + 15) / 16), block, 0, st>>>(
+            xs, wps, bps, wgs, bgs, ms, dos, dpw, dgw, M, K, N);
+        gdp_bwd_generic_dx_kernel<T><<<dim3((K + 15) / 16, (M + 15) / 16), block, 0, st>>>(
+            dpw, dgw, wps, wgs, static_cast<uint16_t*>(dx), M, K, N);
+        gdp_bwd_generic_dw_kernel<T><<<dim3((N + 127) / 128, K + 1), 128, 0, st>>>(
+            xs, dpw, dgw, dwp, dwg, dbp, dbg, M, K, N);
+        return check_launch("gdp_bwd_generic");
+    }
+    if (cudaMemsetAsync(dwp, 0, static_cast<size_t>(K) * N * 4, st) != cudaSuccess ||
+        cudaMemsetAsync(dwg, 0, static_cast<size_t>(K) * N * 4, st) != cudaSuccess ||
+        cudaMemsetAsync(dbp, 0, static_cast<size_t>(N) * 4, st) != cudaSuccess ||
+        cudaMemsetAsync(dbg, 0, static_cast<size_t>(N) * 4, st) != cudaSuccess) {
+        return fail(CFK_ERR_LAUNCH, "cfk_gdp_bwd: memset failed");
+    }
+    CUtensorMap tx, twp, twg, tdo, tdo64;
+    CFK_TRY(make_tmap_3d(&tx, x, K, M, 1, 2ull * K, 2ull * K * M, 64, 128, 1, 128, "gdp x"));
+    CFK_TRY(make_tmap_3d(&twp, wp, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wp"));
+    CFK_TRY(make_tmap_3d(&twg, wg, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wg"));
+    CFK_TRY(make_tmap_3d(&tdo, dout, N, M, 1, 2ull * N, 2ull * N * M, 64, 128, 1, 128,
+                         "gdp dout"));
+    tdo64 = tdo;
+    const int n_mt = (M + 127) / 128;
+    {
+        const DxLayout L = dx_layout(K);
+        auto kern = gdp_bwd_dx_kernel<T>;
+        CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
+                                 "gdp_bwd_dx"));
+        const int grid = std::min(n_mt, dev.num_sms);
+        kern<<<grid, kThreads, L.total, st>>>(tx, twp, twg, tdo, bps, bgs, ms,
+                                              static_cast<uint16_t*>(dx), M, K, N);
+        CFK_TRY(check_launch("gdp_bwd_dx"));
+    }
+    {
+        const DwLayout L = dw_layout(K);
+        auto kern = gdp_bwd_dw_kernel<T>;
+        CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
+                                 "gdp_bwd_dw"));
+        const int nch = (N + 63) / 64;
+        const int groups = std::max(1, std::min(n_mt, dev.num_sms / nch));
+        kern<<<nch * groups, kThreads, L.total, st>>>(tx, twp, twg, tdo64, bps, bgs, ms, dwp,
+                                                      dwg, dbp, dbg, M, K, N, groups);
+        CFK_TRY(check_launch("gdp_bwd_dw"));
+    }
+    return CFK_OK;
+}
+
+} // namespace
+} // namespace gdp
+} // namespace cfk
+
+using namespace cfk;
+
+namespace {
+int check_gdp_args(const char* fn, int dtype, int64_t M, int64_t K, int64_t N) {
+    if (dtype != CFK_F16 && dtype != CFK_BF16) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "%s: dtype must be CFK_F16 or CFK_BF16", fn);
+    }
+    if (M < 0 || K <= 0 || N <= 0) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "%s: x must be [M,K], wp/wg [K,N] with K, N > 0",
+                    fn);
+    }
+    // cuda/volta_ops.cu:234-236
+    if (N % 8) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "%s: N must be a multiple of 8", fn);
+    }
+    if (M > (1ll << 31) - 1 || K > 65535 || N > 65535) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "%s: tensor too large", fn);
+    }
+    return CFK_OK;
+}
+} // namespace
+
+extern "C" int cfk_gdp_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, const void* wp,
+                           const void* bp, const void* wg, const void* bg, const void* mask,
+                           void* out, int64_t M, int64_t K, int64_t N) {
+    clear_error();
+    CFK_TRY(check_gdp_args("cfk_gdp_fwd", dtype, M, K, N));
+    if (M == 0) {
+        return CFK_OK;
+    }
+    if (!x || !wp || !bp || !wg || !bg || !mask || !out) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_gdp_fwd: null buffer");
+    }
+    DeviceInfo dev;
+    CFK_TRY(current_device(&dev));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    return dtype == CFK_BF16
+               ? gdp::gdp_fwd_impl<__nv_bfloat16>(st, dev, x, wp, bp, wg, bg, mask, out, m, k, n)
+               : gdp::gdp_fwd_impl<__half>(st, dev, x, wp, bp, wg, bg, mask, out, m, k, n);
+}
+
+extern "C" int cfk_gdp_bwd_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes) {
+    clear_error();
+    CFK_TRY(check_gdp_args("cfk_gdp_bwd_workspace_size", CFK_BF16, M, K, N));
+    if (!bytes) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_gdp_bwd_workspace_size: null pointer");
+    }
+    // The tcgen05 path needs none; other shapes keep f32 dp and dg.
+    *bytes = gdp::bwd_fast_shape(K, N) ? 0 : static_cast<size_t>(M * N) * 8;
+    return CFK_OK;
+}
+
+extern "C" int cfk_gdp_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, const void* wp,
+                           const void* bp, const void* wg, const void* bg, const void* mask,
+                           const void* dout, void* dx, float* dwp, float* dbp, float* dwg,
+                           float* dbg, void* workspace, size_t workspace_bytes, int64_t M,
+                           int64_t K, int64_t N) {
+    clear_error();
+    CFK_TRY(check_gdp_args("cfk_gdp_bwd", dtype, M, K, N));
+    if (!wp || !bp || !wg || !bg || !dwp || !dbp || !dwg || !dbg) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_gdp_bwd: null buffer");
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (M == 0) {
+        cudaError_t e = cudaMemsetAsync(dwp, 0, static_cast<size_t>(K * N) * 4, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(dwg, 0, static_cast<size_t>(K * N) * 4, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(dbp, 0, static_cast<size_t>(N) * 4, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(dbg, 0, static_cast<size_t>(N) * 4, st);
+        return e == cudaSuccess ? CFK_OK : fail(CFK_ERR_LAUNCH, "cfk_gdp_bwd: memset failed");
+    }
+    if (!x || !mask || !dout || !dx) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_gdp_bwd: null buffer");
+    }
+    DeviceInfo dev;
+    CFK_TRY(current_device(&dev));
+    const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    return dtype == CFK_BF16
+               ? gdp::gdp_bwd_impl<__nv_bfloat16>(st, dev, x, wp, bp, wg, bg, mask, dout, dx, dwp,
+                                                  dbp, dwg, dbg, workspace, workspace_bytes, m, k,
+                                                  n)
+               : gdp::gdp_bwd_impl<__half>(st, dev, x, wp, bp, wg, bg, mask, dout, dx, dwp, dbp,
+                                           dwg, dbg, workspace, workspace_bytes, m, k, n);
+}

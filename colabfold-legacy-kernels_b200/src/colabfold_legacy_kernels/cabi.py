@@ -47,6 +47,8 @@ SIGNATURES = {
     "cfk_attn_bwd_workspace_size": [_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_sz)],
     "cfk_attn_bwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                      _vp, _sz, _i64, _i64, _i64, _i64, _i64, _f32],
+    "cfk_attn_bwd_phase": [_int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                           _vp, _vp, _vp, _sz, _i64, _i64, _i64, _i64, _i64, _f32],
     "cfk_ln_fwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32],
     "cfk_ln_bwd_workspace_size": [_i64, _i64, ctypes.POINTER(_sz)],
     "cfk_ln_bwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64,

@@ -57,8 +57,13 @@ def attention_bwd_workspace(n, h, sq, sk, d, device):
     return torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device)
 
 
-def attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=None, grads=None):
-    """(dq, dk, dv, dbias) of attention_fwd; dbias is f32 [H,Sq,Sk]."""
+def attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=None, grads=None,
+                  phase=None):
+    """(dq, dk, dv, dbias) of attention_fwd; dbias is f32 [H,Sq,Sk].
+
+    phase=None runs the whole backward; phase 0, 1 or 2 runs one of its launches
+    (cfk_attn_bwd_phase), in which case `workspace` and `grads` must be passed to every phase.
+    """
     _check(q, k, v, bias, kmask, out, lse, dout)
     n, h, sq, d = q.shape
     sk = k.shape[2]
@@ -68,11 +73,14 @@ def attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=None, g
     dq, dk, dv, dbias = grads
     if workspace is None:
         workspace = attention_bwd_workspace(n, h, sq, sk, d, q.device)
+    args = (_stream(q.device), _dtype_code(q), _ptr(q), _ptr(k), _ptr(v), _ptr(bias),
+            _ptr(kmask), _ptr(out), _ptr(lse), _ptr(dout), _ptr(dq), _ptr(dk), _ptr(dv),
+            _ptr(dbias), _ptr(workspace), workspace.numel(), n, h, sq, sk, d, float(scale))
     with torch.cuda.device(q.device):
-        cabi.call("cfk_attn_bwd", _stream(q.device), _dtype_code(q), _ptr(q), _ptr(k), _ptr(v),
-                  _ptr(bias), _ptr(kmask), _ptr(out), _ptr(lse), _ptr(dout), _ptr(dq), _ptr(dk),
-                  _ptr(dv), _ptr(dbias), _ptr(workspace), workspace.numel(), n, h, sq, sk, d,
-                  float(scale))
+        if phase is None:
+            cabi.call("cfk_attn_bwd", *args)
+        else:
+            cabi.call("cfk_attn_bwd_phase", int(phase), *args)
     return dq, dk, dv, dbias
 
 
