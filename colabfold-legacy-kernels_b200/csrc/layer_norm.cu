@@ -10,6 +10,7 @@
 // statistics need only log2(LPR) shuffles.  Each warp keeps U row groups in flight to cover
 // DRAM latency.  Any other C takes a warp-per-row path with scalar accesses.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "host.h"
@@ -641,4 +642,139 @@ extern "C" int cfk_ln_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* x,
                                                           dgamma, dbeta, partial, M, C, eps)
                              : ln_bwd_impl<__half>(st, d, x, gamma, mean, rstd, dy, dx, dgamma,
                                                    dbeta, partial, M, C, eps);
+}
+
+// ------------------------------------------------------------------------------------------
+// LayerNorm backward without caller-provided scratch.
+//
+// Some callers cannot hand the library device memory: an XLA FFI handler receives only the
+// buffers its binding declares and must not allocate, so a LayerNorm-backward handler with the
+// reference's buffer list (no workspace result) has nowhere to put the per-CTA dgamma/dbeta
+// partials; hosts that pre-plan every device allocation are in the same position.  For them
+// this variant keeps the partials in a fixed device array that belongs to the library.
+// ------------------------------------------------------------------------------------------
+namespace cfk {
+namespace {
+
+constexpr int kNoAllocMaxC = 1024;    // widest row the static scratch serves
+constexpr int kNoAllocMaxParts = 320; // CTAs (partials) of one launch
+constexpr size_t kNoAllocFloats = static_cast<size_t>(kNoAllocMaxParts) * 2 * kNoAllocMaxC;
+
+// 2.5 MiB per device that loads the library, held until the process exits.  Shared by every
+// call: each launch overwrites the partials it reads, so nothing needs clearing between calls,
+// but two calls that overlap on the GPU (different streams, same device) race on it.
+static __device__ __align__(256) float g_ln_noalloc_scratch[kNoAllocFloats];
+
+constexpr int kMaxDev = 64;
+std::once_flag g_noalloc_once[kMaxDev];
+float* g_noalloc_ptr[kMaxDev];
+cudaError_t g_noalloc_err[kMaxDev];
+
+// Device address of the scratch on the current device.  The array's name is only a host-side
+// stand-in, so the address comes from cudaGetSymbolAddress, once per device, with that device
+// current.
+int noalloc_scratch(int dev, float** out) {
+    std::call_once(g_noalloc_once[dev], [dev]() {
+        void* p = nullptr;
+        g_noalloc_err[dev] = cudaGetSymbolAddress(&p, g_ln_noalloc_scratch);
+        g_noalloc_ptr[dev] = static_cast<float*>(p);
+    });
+    if (g_noalloc_err[dev] != cudaSuccess || !g_noalloc_ptr[dev]) {
+        return fail(CFK_ERR_LAUNCH, "cfk_ln_bwd_noalloc: cudaGetSymbolAddress failed: %s",
+                    cudaGetErrorString(g_noalloc_err[dev]));
+    }
+    *out = g_noalloc_ptr[dev];
+    return CFK_OK;
+}
+
+template <typename T>
+int ln_bwd_noalloc_impl(cudaStream_t st, const DeviceInfo& d, const void* x, const float* gamma,
+                        const float* mean, const float* rstd, const void* dy, void* dx,
+                        float* dgamma, float* dbeta, float* partial, int64_t M, int64_t C,
+                        float eps) {
+    VecShape s;
+    const T* xp = static_cast<const T*>(x);
+    const T* dyp = static_cast<const T*>(dy);
+    T* dxp = static_cast<T*>(dx);
+    int grid = 0;
+    bool launched = false;
+    if (vec_shape(C, &s) && aligned16(x) && aligned16(dy) && aligned16(dx)) {
+        const int64_t rps = static_cast<int64_t>(32 / s.lpr) * kU;
+        grid = std::min(grid_for((M + rps - 1) / rps, d), kNoAllocMaxParts);
+#define CFK_LN_BWD_NA(LPR, NV)                                                                     \
+    if (!launched && s.lpr == LPR && s.nv == NV) {                                                 \
+        ln_bwd_vec_kernel<T, LPR, NV, kU>                                                          \
+            <<<grid, kThreads, 0, st>>>(xp, gamma, mean, rstd, dyp, dxp, partial, M, eps);         \
+        launched = true;                                                                           \
+    }
+        CFK_LN_BWD_NA(8, 1)
+        CFK_LN_BWD_NA(16, 1)
+        CFK_LN_BWD_NA(32, 1)
+        CFK_LN_BWD_NA(16, 3)
+        CFK_LN_BWD_NA(32, 2)
+        CFK_LN_BWD_NA(32, 3)
+        CFK_LN_BWD_NA(32, 4)
+#undef CFK_LN_BWD_NA
+    }
+    if (!launched) {
+        grid = std::min(grid_for(M, d), kNoAllocMaxParts);
+        const int smem = kWarps * 2 * static_cast<int>(C) * static_cast<int>(sizeof(float));
+        if (smem > 48 * 1024) {
+            CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(&ln_bwd_generic_kernel<T>),
+                                     d.device, smem, "ln_bwd_noalloc"));
+        }
+        ln_bwd_generic_kernel<T><<<grid, kThreads, smem, st>>>(xp, gamma, mean, rstd, dyp, dxp,
+                                                               partial, M, static_cast<int>(C), eps);
+    }
+    CFK_TRY(check_launch("ln_bwd_noalloc"));
+    const int threads = 256;
+    const int blocks = static_cast<int>((2 * C + threads - 1) / threads);
+    ln_bwd_reduce_kernel<<<blocks, threads, 0, st>>>(partial, grid, static_cast<int>(C), dgamma,
+                                                     dbeta);
+    return check_launch("ln_bwd_noalloc_reduce");
+}
+
+} // namespace
+} // namespace cfk
+
+extern "C" int cfk_ln_bwd_noalloc(cfk_stream_t stream, cfk_dtype dtype, const void* x,
+                                  const float* gamma, const float* mean, const float* rstd,
+                                  const void* dy, void* dx, float* dgamma, float* dbeta,
+                                  int64_t M, int64_t C, float eps) {
+    clear_error();
+    CFK_TRY(check_ln_args("cfk_ln_bwd_noalloc", dtype, M, C, eps));
+    if (C > kNoAllocMaxC) {
+        return fail(CFK_ERR_INVALID_ARGUMENT,
+                    "cfk_ln_bwd_noalloc: C=%lld exceeds the %d columns its static scratch serves; "
+                    "use cfk_ln_bwd with a workspace",
+                    static_cast<long long>(C), kNoAllocMaxC);
+    }
+    if (!gamma || !dgamma || !dbeta) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_ln_bwd_noalloc: null buffer");
+    }
+    if ((mean == nullptr) != (rstd == nullptr)) {
+        return fail(CFK_ERR_INVALID_ARGUMENT,
+                    "cfk_ln_bwd_noalloc: give both mean and rstd, or neither to recompute them");
+    }
+    DeviceInfo d;
+    CFK_TRY(current_device(&d));
+    float* partial = nullptr;
+    CFK_TRY(noalloc_scratch(d.device, &partial));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (M == 0) {
+        cudaError_t e1 = cudaMemsetAsync(dgamma, 0, C * sizeof(float), st);
+        cudaError_t e2 = cudaMemsetAsync(dbeta, 0, C * sizeof(float), st);
+        if (e1 != cudaSuccess || e2 != cudaSuccess) {
+            return fail(CFK_ERR_LAUNCH, "cfk_ln_bwd_noalloc: memset failed");
+        }
+        return CFK_OK;
+    }
+    if (!x || !dy || !dx) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_ln_bwd_noalloc: null buffer");
+    }
+    return dtype == CFK_BF16
+               ? ln_bwd_noalloc_impl<__nv_bfloat16>(st, d, x, gamma, mean, rstd, dy, dx, dgamma,
+                                                    dbeta, partial, M, C, eps)
+               : ln_bwd_noalloc_impl<__half>(st, d, x, gamma, mean, rstd, dy, dx, dgamma, dbeta,
+                                             partial, M, C, eps);
 }

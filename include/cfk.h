@@ -119,6 +119,22 @@ CFK_API int cfk_ln_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, cons
                float* dbeta, void* workspace, size_t workspace_bytes, int64_t M, int64_t C,
                float eps);
 
+/* LayerNorm backward that allocates nothing and takes no workspace.  It has no counterpart in
+ * the reference.  It is for callers that cannot provide device memory: an XLA FFI handler gets
+ * only the buffers its binding declares and must not allocate, so a handler with the
+ * reference's buffer list (no workspace result) cannot feed cfk_ln_bwd; hosts that plan every
+ * device allocation up front are in the same position.  The per-CTA dgamma/dbeta partials live
+ * in a static device array of 2.5 MiB (held by every GPU that loads the library until the
+ * process exits), so C must be <= 1024 (larger C is rejected with CFK_ERR_INVALID_ARGUMENT).
+ * The first call on a device looks up the array's device address with that device current;
+ * make that first call before any stream capture.  All calls share the array: each launch
+ * rewrites the partials it reads, so nothing carries over, but calls that overlap on the GPU
+ * (for example on two streams of one device) race.  Results equal cfk_ln_bwd's up to the
+ * summation order of dgamma and dbeta. */
+CFK_API int cfk_ln_bwd_noalloc(cfk_stream_t stream, cfk_dtype dtype, const void* x,
+                       const float* gamma, const float* mean, const float* rstd, const void* dy,
+                       void* dx, float* dgamma, float* dbeta, int64_t M, int64_t C, float eps);
+
 /* ------------------------------------------------------------------------------------------ */
 /* Gated dual projection:                                                                     */
 /*   out[m,n] = mask[m] * (x@wp + bp)[m,n] * sigmoid((x@wg + bg)[m,n])                        */
