@@ -460,15 +460,16 @@ __global__ void __launch_bounds__(320, 1)
             }
             for (int b = b_lo; b < b_hi; ++b, ++g) {
                 const int s = g % NST;
+                // row statistics first: their latency overlaps the wait for S and dP
+                const int64_t lrow = (static_cast<int64_t>(b) * p.H + h) * p.Sq + row;
+                const float lse = row_ok ? p.lse[lrow] : 0.f;
+                const float delta = row_ok ? p.delta[lrow] : 0.f;
                 if (!mbar_wait(sdp_full, g & 1, abort_flag) ||
                     !mbar_wait(&kv_full[s], (g / NST) & 1, abort_flag)) {
                     goto done;
                 }
                 __syncwarp();
                 tc_fence_after();
-                const int64_t lrow = (static_cast<int64_t>(b) * p.H + h) * p.Sq + row;
-                const float lse = row_ok ? p.lse[lrow] : 0.f;
-                const float delta = row_ok ? p.delta[lrow] : 0.f;
                 const float lseL = lse * kLog2e;
                 const bool select = flag_all[s] != 0 && (always_select || lse < kMaskedLogit + 104.f);
                 const float p_masked = ex2((kMaskedLogit - lse) * kLog2e);
@@ -502,27 +503,38 @@ __global__ void __launch_bounds__(320, 1)
                         }
                     }
                     uint32_t pk[8], dk[8];
+                    const float2 scale2 = make_float2(scale, scale);
+                    const float2 l2 = make_float2(kLog2e, kLog2e);
+                    const float2 nlse2 = make_float2(-lseL, -lseL);
+                    const float2 ndelta2 = make_float2(-delta, -delta);
 #pragma unroll
                     for (int k = 0; k < 16; k += 2) {
-                        float pr[2], dsr[2];
-#pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const float t = fmaf(__uint_as_float(sv[k + e]), scale, bvals[k + e]);
-                            float pv = ex2(fmaf(t, kLog2e, -lseL));
-                            float dsv = pv * (__uint_as_float(dpv[k + e]) - delta);
-                            if (select) {
-                                const uint8_t code = keep[16 * c + k + e];
-                                if (code != 2) {
-                                    pv = (code == 1) ? p_masked : 0.f;
-                                    dsv = 0.f;
-                                }
+                        const float2 t2 = ffma2(make_float2(__uint_as_float(sv[k]),
+                                                            __uint_as_float(sv[k + 1])),
+                                                scale2, make_float2(bvals[k], bvals[k + 1]));
+                        const float2 a2 = ffma2(t2, l2, nlse2);
+                        float2 p2 = make_float2(ex2(a2.x), ex2(a2.y));
+                        const float2 d2 = fadd2(make_float2(__uint_as_float(dpv[k]),
+                                                            __uint_as_float(dpv[k + 1])),
+                                                ndelta2);
+                        float2 ds2 = fmul2(p2, d2);
+                        if (select) {
+                            const uint8_t c0 = keep[16 * c + k], c1 = keep[16 * c + k + 1];
+                            if (c0 != 2) {
+                                p2.x = (c0 == 1) ? p_masked : 0.f;
+                                ds2.x = 0.f;
                             }
-                            pr[e] = pv;
-                            dsr[e] = dsv;
-                            dbias[16 * c + k + e] += dsv;
+                            if (c1 != 2) {
+                                p2.y = (c1 == 1) ? p_masked : 0.f;
+                                ds2.y = 0.f;
+                            }
                         }
-                        pk[k / 2] = E::pack(pr[0], pr[1]);
-                        dk[k / 2] = E::pack(dsr[0], dsr[1]);
+                        const float2 db2 = fadd2(make_float2(dbias[16 * c + k],
+                                                             dbias[16 * c + k + 1]), ds2);
+                        dbias[16 * c + k] = db2.x;
+                        dbias[16 * c + k + 1] = db2.y;
+                        pk[k / 2] = E::pack(p2.x, p2.y);
+                        dk[k / 2] = E::pack(ds2.x, ds2.y);
                     }
                     if (c == 0 && g > 0) {
                         // the previous step's partial-sum MMAs must be done reading P and dS

@@ -11,11 +11,15 @@
 //                  tiles of every batch row, the bias tile [128 x 128] (shared by the NWG
 //                  rows), and the key-mask operand described below.
 //   warp NWG*4+1   MMA issuer (one thread): S_w = q_w k_w^T + ones * maskcol_w^T into tensor
-//                  memory, then O_w = P_w v_w with P read from tensor memory.
-//   warpgroup w    softmax of batch row w of the item: thread r owns query row r.  It loads
-//                  its 128 scores from tensor memory, adds scale and bias, keeps the running
-//                  max and sum, writes P (16-bit) back over the scores, and accumulates the
-//                  O tile that the MMA writes in registers.
+//                  memory, then O_w += P_w v_w per 64-key half, P read from tensor memory.
+//   warpgroup w    softmax of batch row w of the item: thread r owns query row r.  It works
+//                  on each 128-key tile in two 64-key halves: loads the half's scores from
+//                  tensor memory, adds scale and bias, keeps the running max and sum, and
+//                  writes that half's P (16-bit) to its own tensor-memory columns, whose P V the
+//                  MMA warp starts while the second half is computed.  Once both halves of S are
+//                  in registers, the MMA warp may write the next tile's S.
+//
+// Tensor memory per warpgroup (256 columns): S [128] | P half 0 [32] | P half 1 [32] | O [Dp].
 //
 // Masked keys cost no per-score work in the common case: a second K=16 MMA adds
 // ones[128 x 16] * maskcol^T, where maskcol[j, 0] = -big for a masked or out-of-range key and 0
@@ -39,9 +43,10 @@ struct FwdCfg {
     static constexpr int kThreads = NWG * 128 + 64;
     static constexpr int kProducerWarp = NWG * 4;
     static constexpr int kMmaWarp = NWG * 4 + 1;
-    static constexpr uint32_t kTmemCols = NWG == 2 ? 512 : 256; // S/P 128 + O Dp per group
-    static constexpr int kSCol = 0;   // S/P of warpgroup w at w*256
-    static constexpr int kOCol = 128; // O accumulator of warpgroup w at w*256 + 128
+    static constexpr uint32_t kTmemCols = NWG == 2 ? 512 : 256;
+    static constexpr int kSCol = 0;   // S of warpgroup w at w*256
+    static constexpr int kPCol = 128; // P half h (16-bit pairs, 32 columns) at w*256 + 128 + 32h
+    static constexpr int kOCol = 192; // O accumulator (Dp columns) at w*256 + 192
 
     static constexpr int kTile = ((G::kTileAlloc + 1023) / 1024) * 1024;
     static constexpr int kBiasBytes = 128 * 128 * 2;
@@ -58,13 +63,22 @@ struct FwdCfg {
     static constexpr int kOffKeep = kOffOnes + kMaskOpBytes;          // u8 [NST][NWG][128]
     static constexpr int kOffFlag = kOffKeep + NST * NWG * 128;        // u32 [NST][NWG]
     static constexpr int kOffBar = ((kOffFlag + NST * NWG * 4 + 7) / 8) * 8;
-    // barriers: q_full[NWG], q_empty[NWG], kv_full[NST], kv_empty[NST], s_full[NWG],
-    // p_full[NWG], o_full[NWG]
-    static constexpr int kNumBars = 5 * NWG + 2 * NST;
+    // barriers (index): q_full[w] 0.., q_empty[w], kv_full[s], kv_empty[s], s_full[w],
+    // s_free[w], p_full[w][2], o_full[w][2]
+    static constexpr int kBarQFull = 0;
+    static constexpr int kBarQEmpty = NWG;
+    static constexpr int kBarKvFull = 2 * NWG;
+    static constexpr int kBarKvEmpty = 2 * NWG + NST;
+    static constexpr int kBarSFull = 2 * NWG + 2 * NST;
+    static constexpr int kBarSFree = kBarSFull + NWG;
+    static constexpr int kBarPFull = kBarSFree + NWG;  // + 2w + h
+    static constexpr int kBarOFull = kBarPFull + 2 * NWG; // + 2w + h
+    static constexpr int kNumBars = kBarOFull + 2 * NWG;
     static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
     static constexpr int kOffAbort = kOffTmemSlot + 4;
     static constexpr int kSmemBytes = kOffAbort + 4 + 1024; // + alignment slack
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+    static_assert(kOCol + G::kDp <= 256, "tensor memory budget");
 
     static constexpr uint32_t kStageTx = 2 * NWG * G::kTileBytes; // + bias when by TMA
 };
@@ -97,18 +111,14 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
     const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar0 = sbase + C::kOffBar; // barrier i at bar0 + 8 i
+    const uint32_t abort_s = sbase + C::kOffAbort;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
-    uint64_t* q_full = bars;
-    uint64_t* q_empty = bars + NWG;
-    uint64_t* kv_full = bars + 2 * NWG;
-    uint64_t* kv_empty = bars + 2 * NWG + NST;
-    uint64_t* s_full = bars + 2 * NWG + 2 * NST;
-    uint64_t* p_full = s_full + NWG;
-    uint64_t* o_full = p_full + NWG;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + C::kOffAbort);
     uint8_t* keep_all = smem + C::kOffKeep;
     uint32_t* flag_all = reinterpret_cast<uint32_t*>(smem + C::kOffFlag);
+    auto BAR = [bar0](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -116,15 +126,18 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
     // ---- one-time set-up ----
     if (threadIdx.x == 0) {
         for (int w = 0; w < NWG; ++w) {
-            mbar_init(&q_full[w], 1);
-            mbar_init(&q_empty[w], 1);
-            mbar_init(&s_full[w], 1);
-            mbar_init(&p_full[w], 4);
-            mbar_init(&o_full[w], 1);
+            mbar_init(&bars[C::kBarQFull + w], 1);
+            mbar_init(&bars[C::kBarQEmpty + w], 1);
+            mbar_init(&bars[C::kBarSFull + w], 1);
+            mbar_init(&bars[C::kBarSFree + w], 4);
+            for (int h = 0; h < 2; ++h) {
+                mbar_init(&bars[C::kBarPFull + 2 * w + h], 4);
+                mbar_init(&bars[C::kBarOFull + 2 * w + h], 1);
+            }
         }
         for (int s = 0; s < NST; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1 + 4 * NWG);
+            mbar_init(&bars[C::kBarKvFull + s], 2); // TMA bytes + mask operand
+            mbar_init(&bars[C::kBarKvEmpty + s], 1 + 4 * NWG);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -197,34 +210,29 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
             const int q0 = qt * kBM;
             for (int w = 0; w < NWG; ++w) {
                 const int b = grp * NWG + w;
-                if (it > 0 && !mbar_wait(&q_empty[w], (it - 1) & 1, abort_flag)) {
+                if (it > 0 && !mbar_wait_s(BAR(C::kBarQEmpty + w), (it - 1) & 1, abort_s)) {
                     goto done;
                 }
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&q_full[w], G::kTileBytes);
-                    tma_load_3d(smem + C::kOffQ + w * C::kTile, &tm_q, &q_full[w], 0, q0,
-                                b * p.H + h);
+                    mbar_arrive_expect_tx(&bars[C::kBarQFull + w], G::kTileBytes);
+                    tma_load_3d(smem + C::kOffQ + w * C::kTile, &tm_q, &bars[C::kBarQFull + w], 0,
+                                q0, b * p.H + h);
                 }
             }
             for (int t = 0; t < p.n_kt; ++t, ++g) {
                 const int s = g % NST;
-                if (g >= NST && !mbar_wait(&kv_empty[s], ((g / NST) - 1) & 1, abort_flag)) {
-                    goto done;
-                }
-                uint8_t* stage = smem + C::kOffStages + s * C::kStageBytes;
                 const int j0 = t * kBN;
-                // key-mask operand and keep codes (0 out of range, 1 masked, 2 kept)
+                // keep codes of this lane's 4 keys per batch row (0 out of range, 1 masked,
+                // 2 kept), read before waiting for the stage so the loads overlap the wait
+                uint32_t codes[NWG];
+#pragma unroll
                 for (int w = 0; w < NWG; ++w) {
                     const int b = grp * NWG + w;
-                    uint16_t* mo = reinterpret_cast<uint16_t*>(stage + C::kOffMaskOp +
-                                                               w * C::kMaskOpBytes);
-                    uint8_t* keep = keep_all + (s * NWG + w) * 128;
-                    bool any_excluded = false;
+                    codes[w] = 0;
 #pragma unroll
                     for (int r = 0; r < 4; ++r) {
-                        const int jj = lane * 4 + r;
-                        const int j = j0 + jj;
-                        uint8_t code;
+                        const int j = j0 + lane * 4 + r;
+                        uint32_t code;
                         if (j >= p.Sk) {
                             code = 0;
                         } else if (b >= p.N) {
@@ -232,35 +240,57 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                         } else {
                             code = p.kmask[static_cast<int64_t>(b) * p.Sk + j] ? 2 : 1;
                         }
-                        keep[jj] = code;
-                        mo[jj * 8] = (code == 2 || p.mask_bits == 0) ? uint16_t(0)
-                                                                     : uint16_t(p.mask_bits);
+                        codes[w] |= code << (8 * r);
+                    }
+                }
+                if (g >= NST &&
+                    !mbar_wait_s(BAR(C::kBarKvEmpty + s), ((g / NST) - 1) & 1, abort_s)) {
+                    goto done;
+                }
+                uint8_t* stage = smem + C::kOffStages + s * C::kStageBytes;
+                uint64_t* full = &bars[C::kBarKvFull + s];
+                // the tiles first (first of the two arrivals), then the mask operand
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(full, C::kStageTx + (kBiasTma ? C::kBiasBytes : 0));
+                    for (int w = 0; w < NWG; ++w) {
+                        const int b = grp * NWG + w;
+                        tma_load_3d(stage + C::kOffK + w * C::kTile, &tm_k, full, 0, j0,
+                                    b * p.H + h);
+                        tma_load_3d(stage + C::kOffV + w * C::kTile, &tm_v, full, 0, j0,
+                                    b * p.H + h);
+                    }
+                    if constexpr (kBiasTma) {
+                        tma_load_3d(stage + C::kOffBias, &tm_bias, full, j0, q0, h);
+                        tma_load_3d(stage + C::kOffBias + 16384, &tm_bias, full, j0 + 64, q0, h);
+                    }
+                }
+#pragma unroll
+                for (int w = 0; w < NWG; ++w) {
+                    uint16_t* mo = reinterpret_cast<uint16_t*>(stage + C::kOffMaskOp +
+                                                               w * C::kMaskOpBytes);
+                    uint8_t* keep = keep_all + (s * NWG + w) * 128;
+                    *reinterpret_cast<uint32_t*>(keep + lane * 4) = codes[w];
+                    bool any_excluded = false;
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const uint32_t code = (codes[w] >> (8 * r)) & 0xFFu;
+                        mo[(lane * 4 + r) * 8] = (code == 2 || p.mask_bits == 0)
+                                                     ? uint16_t(0)
+                                                     : uint16_t(p.mask_bits);
                         any_excluded |= (code != 2);
                     }
-                    const uint32_t anyx = __any_sync(0xffffffffu, any_excluded);
+                    // bit h: the 64-key half h holds an excluded key
+                    const uint32_t lo = __any_sync(0xffffffffu, any_excluded && lane < 16);
+                    const uint32_t hi = __any_sync(0xffffffffu, any_excluded && lane >= 16);
                     if (lane == 0) {
-                        flag_all[s * NWG + w] = anyx;
+                        flag_all[s * NWG + w] = (lo ? 1u : 0u) | (hi ? 2u : 0u);
                     }
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&kv_full[s],
-                                          C::kStageTx + (kBiasTma ? C::kBiasBytes : 0));
-                    for (int w = 0; w < NWG; ++w) {
-                        const int b = grp * NWG + w;
-                        tma_load_3d(stage + C::kOffK + w * C::kTile, &tm_k, &kv_full[s], 0, j0,
-                                    b * p.H + h);
-                        tma_load_3d(stage + C::kOffV + w * C::kTile, &tm_v, &kv_full[s], 0, j0,
-                                    b * p.H + h);
-                    }
-                    if constexpr (kBiasTma) {
-                        tma_load_3d(stage + C::kOffBias, &tm_bias, &kv_full[s], j0, q0, h);
-                        tma_load_3d(stage + C::kOffBias + 16384, &tm_bias, &kv_full[s], j0 + 64,
-                                    q0, h);
-                    }
+                    mbar_arrive(full); // second arrival: mask operand and flags written
                 }
-                __syncwarp();
             }
         }
     } else if (warp == C::kMmaWarp) {
@@ -270,38 +300,48 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
             constexpr uint32_t kIdMask = idesc_f16(128, 128, false, false, true);
             constexpr uint32_t kIdPV = idesc_f16(128, G::kDp, false, true, E::kBf16);
             const uint64_t ones_desc = interleave16_kmajor(sbase + C::kOffOnes);
+            // P V of half `hf` of global tile gp for warpgroup w (V from stage gp % NST);
+            // `first`: tile gp is the first of its item, so half 0 overwrites O
+            auto issue_pv = [&](int w, uint32_t gp, int hf, bool first) -> bool {
+                if (!mbar_wait_s(BAR(C::kBarPFull + 2 * w + hf), gp & 1, abort_s)) {
+                    return false;
+                }
+                tc_fence_after();
+                const uint32_t vb = sbase + C::kOffStages + (gp % NST) * C::kStageBytes +
+                                    C::kOffV + w * C::kTile;
+                const uint32_t p_tm = tmem + w * 256 + C::kPCol + 32 * hf;
+                const uint32_t o_tm = tmem + w * 256 + C::kOCol;
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    umma_ts(o_tm, p_tm + ks * 8, G::mnmajor(vb, 4 * hf + ks), kIdPV,
+                            (!first || hf > 0 || ks > 0) ? 1u : 0u);
+                }
+                umma_commit(&bars[C::kBarOFull + 2 * w + hf]);
+                return true;
+            };
+            // One flat sequence over the tiles of all items: S(g) once the softmax has read
+            // S(g-1), then P V of the second half of tile g-1, then of the first half of g.
             uint32_t g = 0;
-            int sp = 0;
+            bool prev_first = false; // tile g - 1 was the first tile of its item
             for (int it = 0; it < n_items_mine; ++it) {
                 for (int w = 0; w < NWG; ++w) {
-                    if (!mbar_wait(&q_full[w], it & 1, abort_flag)) {
+                    if (!mbar_wait_s(BAR(C::kBarQFull + w), it & 1, abort_s)) {
                         goto done;
                     }
                 }
                 for (int t = 0; t < p.n_kt; ++t, ++g) {
                     const int s = g % NST;
-                    if (!mbar_wait(&kv_full[s], (g / NST) & 1, abort_flag)) {
+                    if (!mbar_wait_s(BAR(C::kBarKvFull + s), (g / NST) & 1, abort_s)) {
                         goto done;
                     }
                     tc_fence_after();
                     const uint32_t stage = sbase + C::kOffStages + s * C::kStageBytes;
                     for (int w = 0; w < NWG; ++w) {
-                        const uint32_t s_tm = tmem + w * 256 + C::kSCol;
-                        const uint32_t o_tm = tmem + w * 256 + C::kOCol;
-                        if (t > 0) {
-                            if (!mbar_wait(&p_full[w], (g - 1) & 1, abort_flag)) {
-                                goto done;
-                            }
-                            tc_fence_after();
-                            const uint32_t vb = sbase + C::kOffStages + sp * C::kStageBytes +
-                                                C::kOffV + w * C::kTile;
-#pragma unroll
-                            for (int ks = 0; ks < kBN / 16; ++ks) {
-                                umma_ts(o_tm, s_tm + ks * 8, G::mnmajor(vb, ks), kIdPV,
-                                        (t > 1 || ks > 0) ? 1u : 0u);
-                            }
-                            umma_commit(&o_full[w]);
+                        if (g > 0 && !mbar_wait_s(BAR(C::kBarSFree + w), (g - 1) & 1, abort_s)) {
+                            goto done;
                         }
+                        tc_fence_after();
+                        const uint32_t s_tm = tmem + w * 256 + C::kSCol;
                         const uint32_t qb = sbase + C::kOffQ + w * C::kTile;
                         const uint32_t kb = stage + C::kOffK + w * C::kTile;
 #pragma unroll
@@ -311,36 +351,36 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                         umma_ss(s_tm, ones_desc,
                                 interleave16_kmajor(stage + C::kOffMaskOp + w * C::kMaskOpBytes),
                                 kIdMask, 1);
-                        umma_commit(&s_full[w]);
-                    }
-                    if (t > 0) {
-                        umma_commit(&kv_empty[sp]);
+                        umma_commit(&bars[C::kBarSFull + w]);
                     }
                     if (t == p.n_kt - 1) {
                         for (int w = 0; w < NWG; ++w) {
-                            umma_commit(&q_empty[w]);
+                            umma_commit(&bars[C::kBarQEmpty + w]);
                         }
                     }
-                    sp = s;
+                    if (g > 0) {
+                        for (int w = 0; w < NWG; ++w) {
+                            if (!issue_pv(w, g - 1, 1, prev_first)) {
+                                goto done;
+                            }
+                        }
+                        umma_commit(&bars[C::kBarKvEmpty + (g - 1) % NST]);
+                    }
+                    for (int w = 0; w < NWG; ++w) {
+                        if (!issue_pv(w, g, 0, t == 0)) {
+                            goto done;
+                        }
+                    }
+                    prev_first = (t == 0);
                 }
-                // P V of the item's last key tile
+            }
+            if (g > 0) {
                 for (int w = 0; w < NWG; ++w) {
-                    if (!mbar_wait(&p_full[w], (g - 1) & 1, abort_flag)) {
+                    if (!issue_pv(w, g - 1, 1, prev_first)) {
                         goto done;
                     }
-                    tc_fence_after();
-                    const uint32_t s_tm = tmem + w * 256 + C::kSCol;
-                    const uint32_t o_tm = tmem + w * 256 + C::kOCol;
-                    const uint32_t vb =
-                        sbase + C::kOffStages + sp * C::kStageBytes + C::kOffV + w * C::kTile;
-#pragma unroll
-                    for (int ks = 0; ks < kBN / 16; ++ks) {
-                        umma_ts(o_tm, s_tm + ks * 8, G::mnmajor(vb, ks), kIdPV,
-                                (p.n_kt > 1 || ks > 0) ? 1u : 0u);
-                    }
-                    umma_commit(&o_full[w]);
                 }
-                umma_commit(&kv_empty[sp]);
+                umma_commit(&bars[C::kBarKvEmpty + (g - 1) % NST]);
             }
         }
     } else {
@@ -349,8 +389,12 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
         const int r = static_cast<int>(warp_lane_base()) + lane; // query row within the tile
         const uint32_t lane_off = warp_lane_base() << 16;
         const uint32_t s_tm = tmem + lane_off + w * 256 + C::kSCol;
+        const uint32_t p_tm = tmem + lane_off + w * 256 + C::kPCol;
         const uint32_t o_tm = tmem + lane_off + w * 256 + C::kOCol;
+        const uint32_t flag_s = sbase + C::kOffFlag;
         const float scale = p.scale;
+        const float2 scale2 = make_float2(scale, scale);
+        const float2 log2e2 = make_float2(kLog2e, kLog2e);
         const bool always_select = (p.mask_bits == 0);
         uint32_t g = 0;
         for (int it = 0; it < n_items_mine; ++it) {
@@ -362,127 +406,170 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
             const int b = grp * NWG + w;
             const int row = qt * kBM + r;
 
-            // m_run is the max that P is scaled by.  It is raised lazily, only when the tile max
-            // exceeds it by more than ln(256) (P then stays <= 256), which makes the rescale of
-            // O and l rare.
+            // m_run is the max that P is scaled by.  It is raised lazily, only when a half-tile
+            // max exceeds it by more than ln(256) (P then stays <= 256), which makes the rescale
+            // of O and l rare.
             float m_run = -INFINITY, l_run = 0.f;
             for (int t = 0; t < p.n_kt; ++t, ++g) {
                 const int s = g % NST;
-                if (!mbar_wait(&s_full[w], g & 1, abort_flag) ||
-                    !mbar_wait(&kv_full[s], (g / NST) & 1, abort_flag)) {
+                if (!mbar_wait_s(BAR(C::kBarSFull + w), g & 1, abort_s) ||
+                    !mbar_wait_s(BAR(C::kBarKvFull + s), (g / NST) & 1, abort_s)) {
                     goto done;
                 }
                 __syncwarp();
                 tc_fence_after();
-                float x[kBN];
+                const uint32_t flags = ld_shared_u32(flag_s + 4 * (s * NWG + w));
+#pragma unroll 1
+                for (int hf = 0; hf < 2; ++hf) {
+                    float x[64];
+                    {
+                        uint32_t v[32];
+                        tmem_ld32(s_tm + 64 * hf, v);
 #pragma unroll
-                for (int c = 0; c < kBN / 32; ++c) {
-                    uint32_t v[32];
-                    tmem_ld32(s_tm + c * 32, v);
+                        for (int i = 0; i < 32; ++i) {
+                            x[i] = __uint_as_float(v[i]);
+                        }
+                        tmem_ld32(s_tm + 64 * hf + 32, v);
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        x[c * 32 + i] = __uint_as_float(v[i]);
-                    }
-                }
-                tmem_ld_wait();
-                // logit = scale * s + bias (natural-log units)
-                if constexpr (kBiasTma) {
-                    const uint32_t bias_s =
-                        sbase + C::kOffStages + s * C::kStageBytes + C::kOffBias;
-#pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        const uint4 bw = lds128(bias_s + sw128_chunk(r, c));
-                        const uint32_t wv[4] = {bw.x, bw.y, bw.z, bw.w};
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            const float2 bf = E::to_float2(wv[q]);
-                            x[c * 8 + 2 * q] = fmaf(x[c * 8 + 2 * q], scale, bf.x);
-                            x[c * 8 + 2 * q + 1] = fmaf(x[c * 8 + 2 * q + 1], scale, bf.y);
+                        for (int i = 0; i < 32; ++i) {
+                            x[32 + i] = __uint_as_float(v[i]);
                         }
                     }
-                } else {
-                    const int64_t brow =
-                        (static_cast<int64_t>(h) * p.Sq + (row < p.Sq ? row : 0)) * p.Sk;
-                    const int j0 = t * kBN;
-#pragma unroll
-                    for (int j = 0; j < kBN; ++j) {
-                        const float bv = (j0 + j < p.Sk && row < p.Sq)
-                                             ? E::to_float(p.bias[brow + j0 + j])
-                                             : 0.f;
-                        x[j] = fmaf(x[j], scale, bv);
+                    if (hf == 1) {
+                        // all of S is in registers: the MMA may write the next tile's S
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) {
+                            mbar_arrive_s(BAR(C::kBarSFree + w));
+                        }
                     }
-                }
-                float tmax = x[0];
+                    // logit = scale * s + bias (natural-log units)
+                    if constexpr (kBiasTma) {
+                        const uint32_t bias_s = sbase + C::kOffStages + s * C::kStageBytes +
+                                                C::kOffBias + hf * 16384 + r * 128;
 #pragma unroll
-                for (int j = 1; j < kBN; ++j) {
-                    tmax = fmaxf(tmax, x[j]);
-                }
-                if (flag_all[s * NWG + w] != 0 &&
-                    (always_select || fmaxf(m_run, tmax) < kMaskedLogit + 104.f)) {
-                    // exact path: masked keys -> -1e4, out-of-range keys -> -inf
-                    const uint8_t* keep = keep_all + (s * NWG + w) * 128;
+                        for (int c = 0; c < 8; ++c) {
+                            const uint4 bw = lds128(bias_s + ((c ^ (r & 7)) << 4));
+                            const uint32_t wv[4] = {bw.x, bw.y, bw.z, bw.w};
 #pragma unroll
-                    for (int j = 0; j < kBN; ++j) {
-                        const uint8_t code = keep[j];
-                        x[j] = code == 2 ? x[j] : (code == 1 ? kMaskedLogit : -INFINITY);
+                            for (int q = 0; q < 4; ++q) {
+                                const float2 t2 =
+                                    ffma2(make_float2(x[c * 8 + 2 * q], x[c * 8 + 2 * q + 1]),
+                                          scale2, E::to_float2(wv[q]));
+                                x[c * 8 + 2 * q] = t2.x;
+                                x[c * 8 + 2 * q + 1] = t2.y;
+                            }
+                        }
+                    } else {
+                        const int64_t brow =
+                            (static_cast<int64_t>(h) * p.Sq + (row < p.Sq ? row : 0)) * p.Sk;
+                        const int j0 = t * kBN + 64 * hf;
+#pragma unroll
+                        for (int j = 0; j < 64; ++j) {
+                            const float bv = (j0 + j < p.Sk && row < p.Sq)
+                                                 ? E::to_float(p.bias[brow + j0 + j])
+                                                 : 0.f;
+                            x[j] = fmaf(x[j], scale, bv);
+                        }
                     }
-                    tmax = x[0];
+                    // four independent max chains (short dependency latency)
+                    float mx[4];
 #pragma unroll
-                    for (int j = 1; j < kBN; ++j) {
-                        tmax = fmaxf(tmax, x[j]);
+                    for (int u = 0; u < 4; ++u) {
+                        mx[u] = fmax3(x[16 * u], x[16 * u + 1], x[16 * u + 2]);
+#pragma unroll
+                        for (int j = 3; j < 15; j += 2) {
+                            mx[u] = fmax3(mx[u], x[16 * u + j], x[16 * u + j + 1]);
+                        }
+                        mx[u] = fmaxf(mx[u], x[16 * u + 15]);
                     }
-                }
-                float alpha = 1.f;
-                if (t == 0) {
-                    m_run = tmax;
-                } else if (tmax > m_run + 5.545177444479562f) { // ln(256)
-                    alpha = ex2((m_run - tmax) * kLog2e);
-                    m_run = tmax;
-                }
-                const float mL = (m_run == -INFINITY ? 0.f : m_run) * kLog2e;
-                float rs = 0.f;
+                    float tmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+                    if ((flags >> hf & 1u) &&
+                        (always_select || fmaxf(m_run, tmax) < kMaskedLogit + 104.f)) {
+                        // exact path: masked keys -> -1e4, out-of-range keys -> -inf
+                        const uint8_t* keep = keep_all + (s * NWG + w) * 128 + 64 * hf;
 #pragma unroll
-                for (int c = 0; c < kBN / 32; ++c) {
-                    uint32_t pk[16];
+                        for (int j = 0; j < 64; ++j) {
+                            const uint8_t code = keep[j];
+                            x[j] = code == 2 ? x[j] : (code == 1 ? kMaskedLogit : -INFINITY);
+                        }
+                        tmax = x[0];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float p0 = ex2(fmaf(x[c * 32 + 2 * i], kLog2e, -mL));
-                        const float p1 = ex2(fmaf(x[c * 32 + 2 * i + 1], kLog2e, -mL));
-                        rs += p0 + p1;
-                        pk[i] = E::pack(p0, p1);
+                        for (int j = 1; j < 64; ++j) {
+                            tmax = fmaxf(tmax, x[j]);
+                        }
                     }
-                    tmem_st16(s_tm + c * 16, pk);
-                }
-                l_run = l_run * alpha + rs;
-                // Rescale the O accumulated so far (needs the previous P V to have landed).
-                if (t > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-                    if (!mbar_wait(&o_full[w], (g - 1) & 1, abort_flag)) {
+                    const bool first_half = (t == 0 && hf == 0);
+                    float alpha = 1.f;
+                    if (first_half) {
+                        m_run = tmax;
+                    } else if (tmax > m_run + 5.545177444479562f) { // ln(256)
+                        alpha = ex2((m_run - tmax) * kLog2e);
+                        m_run = tmax;
+                    }
+                    // This half's P columns are free once the previous tile's P V of the same
+                    // half is done; a rescale of O needs every earlier P V done (the latest is
+                    // half 1 of the previous tile, or half 0 of this tile).
+                    if (t > 0 && !mbar_wait_s(BAR(C::kBarOFull + 2 * w + hf), (g - 1) & 1,
+                                              abort_s)) {
                         goto done;
+                    }
+                    const bool rescale = __any_sync(0xffffffffu, alpha != 1.f);
+                    if (rescale) {
+                        const bool ok =
+                            hf == 1 ? mbar_wait_s(BAR(C::kBarOFull + 2 * w), g & 1, abort_s)
+                                    : mbar_wait_s(BAR(C::kBarOFull + 2 * w + 1), (g - 1) & 1,
+                                                  abort_s);
+                        if (!ok) {
+                            goto done;
+                        }
                     }
                     __syncwarp();
                     tc_fence_after();
+                    if (rescale) {
 #pragma unroll
-                    for (int c = 0; c < G::kDp / 16; ++c) {
-                        uint32_t v[16];
-                        tmem_ld16(o_tm + c * 16, v);
-                        tmem_ld_wait();
+                        for (int c = 0; c < G::kDp / 16; ++c) {
+                            uint32_t v[16];
+                            tmem_ld16(o_tm + c * 16, v);
+                            tmem_ld_wait();
 #pragma unroll
-                        for (int d = 0; d < 16; ++d) {
-                            v[d] = __float_as_uint(__uint_as_float(v[d]) * alpha);
+                            for (int d = 0; d < 16; ++d) {
+                                v[d] = __float_as_uint(__uint_as_float(v[d]) * alpha);
+                            }
+                            tmem_st16(o_tm + c * 16, v);
                         }
-                        tmem_st16(o_tm + c * 16, v);
+                    }
+                    const float mL = (m_run == -INFINITY ? 0.f : m_run) * kLog2e;
+                    const float2 nmL2 = make_float2(-mL, -mL);
+                    float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const int j = c * 32 + 2 * i;
+                            const float2 a = ffma2(make_float2(x[j], x[j + 1]), log2e2, nmL2);
+                            const float2 e = make_float2(ex2(a.x), ex2(a.y));
+                            rs2[i & 1] = fadd2(rs2[i & 1], e);
+                            pk[i] = E::pack(e.x, e.y);
+                        }
+                        tmem_st16(p_tm + 32 * hf + c * 16, pk);
+                    }
+                    l_run = l_run * alpha + ((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y));
+                    tmem_st_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive_s(BAR(C::kBarPFull + 2 * w + hf));
+                        if (hf == 1) {
+                            mbar_arrive_s(BAR(C::kBarKvEmpty + s));
+                        }
                     }
                 }
-                tmem_st_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&p_full[w]);
-                    mbar_arrive(&kv_empty[s]);
-                }
             }
-            // O after the item's last P V: normalise and store
-            if (!mbar_wait(&o_full[w], (g - 1) & 1, abort_flag)) {
+            // O after the item's last P V (half 1 of its last tile): normalise and store
+            if (!mbar_wait_s(BAR(C::kBarOFull + 2 * w + 1), (g - 1) & 1, abort_s)) {
                 goto done;
             }
             __syncwarp();

@@ -95,6 +95,56 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     }
 }
 
+// The same operations on a 32-bit shared-memory address (one register instead of a 64-bit
+// generic pointer; used where register pressure matters).
+__device__ __forceinline__ void mbar_arrive_s(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_s(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok)
+                 : "r"(bar), "r"(parity)
+                 : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+static __device__ __noinline__ bool mbar_wait_slow_s(uint32_t bar, uint32_t parity,
+                                                     uint32_t abort) {
+    const unsigned long long t0 = global_ns();
+    while (true) {
+        if (mbar_try_wait_s(bar, parity)) {
+            return true;
+        }
+        if (ld_shared_u32(abort)) {
+            return false;
+        }
+        if (global_ns() - t0 > kWaitLimitNs) {
+            asm volatile("st.shared.u32 [%0], 1;" ::"r"(abort) : "memory");
+            atomicOr(&g_status_word, kStatusTimeoutBarrier);
+            return false;
+        }
+    }
+}
+
+// Waits for the phase with the given parity; gives up like mbar_wait (abort = address of the
+// CTA's abort word).  The slow loop is out of line to keep the caller's registers free.
+__device__ __forceinline__ bool mbar_wait_s(uint32_t bar, uint32_t parity, uint32_t abort) {
+    if (mbar_try_wait_s(bar, parity)) {
+        return true;
+    }
+    return mbar_wait_slow_s(bar, parity, abort);
+}
+
 // ---------------------------------------------------------------------------------------------
 // Proxy fences
 // ---------------------------------------------------------------------------------------------
@@ -310,6 +360,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
                  "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]),
                  "r"(r[13]), "r"(r[14]), "r"(r[15])
                  : "memory");
+}
+
+// Moves registers between the warpgroups of a CTA (all threads of a warpgroup execute it).  The
+// per-thread counts of all warpgroups must add up to the CTA's allocation at launch.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ---------------------------------------------------------------------------------------------

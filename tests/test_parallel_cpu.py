@@ -1,0 +1,116 @@
+"""Row-sharded attention with the dbias all-reduce, on CPU ranks (gloo, world size 2).
+
+The sharding and the reduction are host logic; the per-rank compute is the CPU oracle here (the
+GPU path passes the sm_100a kernels instead).  A second test makes one rank fail before the
+collective and checks that the other rank gets an error instead of hanging.
+"""
+
+import os
+import socket
+import sys
+import traceback
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(3)
+    n, h, s, d = 6, 2, 10, 8
+    q, k, v, dout = (torch.randn(n, h, s, d, generator=g, dtype=torch.float64) for _ in range(4))
+    bias = torch.randn(h, s, s, generator=g, dtype=torch.float64)
+    kmask = (torch.rand(n, s, generator=g) > 0.3).to(torch.uint8)
+    kmask[2] = 0
+    return q, k, v, bias, kmask, dout, 0.35
+
+
+def _worker(rank, world, port, queue, fail_rank):
+    try:
+        sys.path[:0] = [REPO, os.path.join(REPO, "colabfold-legacy-kernels_b200", "src")]
+        import torch.distributed as dist
+        import oracle
+        from colabfold_legacy_kernels.parallel import ShardedAttention, shard_rows
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank,
+                                world_size=world, timeout=timedelta(seconds=15))
+        q, k, v, bias, kmask, dout, scale = _inputs()
+        r0, r1 = shard_rows(q.shape[0], world, rank)
+
+        def fwd(q, k, v, bias, kmask, scale):
+            return oracle.attention_fwd(q, k, v, bias, kmask, scale)
+
+        def bwd(q, k, v, bias, kmask, out, lse, dout, scale):
+            if rank == fail_rank:
+                raise RuntimeError("injected failure on rank %d" % rank)
+            return list(oracle.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale))
+
+        sa = ShardedAttention(fwd=fwd, bwd=bwd)
+        res = sa.step(q[r0:r1], k[r0:r1], v[r0:r1], bias, kmask[r0:r1], dout[r0:r1], scale)
+        out, lse = oracle.attention_fwd(q, k, v, bias, kmask, scale)
+        ref = oracle.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale)
+        errs = {
+            "dq": float((res.dq - ref[0][r0:r1]).abs().max()),
+            "dk": float((res.dk - ref[1][r0:r1]).abs().max()),
+            "dv": float((res.dv - ref[2][r0:r1]).abs().max()),
+            "dbias": float((res.dbias - ref[3]).abs().max()),
+            "out": float((res.out - out[r0:r1]).abs().max()),
+        }
+        queue.put((rank, "ok", errs))
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent; the failing rank exits
+        queue.put((rank, "error", "%s: %s" % (type(e).__name__, e)))
+
+
+def _run(world, fail_rank=None, timeout=120):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue, fail_rank))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        rank, status, payload = queue.get(timeout=timeout)
+        results[rank] = (status, payload)
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return results
+
+
+def test_row_sharding_covers_all_rows():
+    from colabfold_legacy_kernels.parallel import shard_rows
+    for n in (1, 7, 768):
+        for world in (1, 2, 3, 8):
+            spans = [shard_rows(n, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            sizes = [b - a for a, b in spans]
+            assert max(sizes) - min(sizes) <= 1
+
+
+def test_sharded_step_matches_single_process():
+    results = _run(2)
+    for rank in (0, 1):
+        status, errs = results[rank]
+        assert status == "ok", errs
+        for name, err in errs.items():
+            assert err < 1e-12, (rank, name, err)
+
+
+def test_failed_rank_gives_error_not_hang():
+    results = _run(2, fail_rank=1)
+    assert results[1][0] == "error" and "injected" in results[1][1]
+    # the surviving rank's all-reduce ends with an error (peer gone), within the timeout
+    assert results[0][0] == "error", results[0]
