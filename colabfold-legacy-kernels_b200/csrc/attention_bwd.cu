@@ -19,6 +19,8 @@
 //               key-mask operand (as in the forward).
 //   warp 9      MMA issuer: S = q k^T (+ mask), dP = dO v^T; then dV = P^T dO, dK = dS^T q,
 //               dQ = dS k from the P and dS tiles the warpgroups wrote to shared memory.
+#include <type_traits>
+
 #include "attention_common.cuh"
 #include "host.h"
 
@@ -65,8 +67,8 @@ struct BwdCfg {
     static constexpr int kOffFlag = kOffKeep + NST * 128;       // u32 [NST]
     static constexpr int kOffBar = ((kOffFlag + NST * 4 + 7) / 8) * 8;
     // kv_full[NST], kv_empty[NST], bias_full, bias_empty, sdp_full, pds_full, pds_empty,
-    // part_full[NPB], part_empty[NPB]
-    static constexpr int kNumBars = 2 * NST + 5 + 2 * NPB;
+    // part_full[NPB], part_empty[NPB], sdp_free
+    static constexpr int kNumBars = 2 * NST + 6 + 2 * NPB;
     static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
     static constexpr int kOffAbort = kOffTmemSlot + 4;
     static constexpr int kSmemBytes = kOffAbort + 4 + 1024;
@@ -126,6 +128,7 @@ __global__ void __launch_bounds__(320, 1)
     uint64_t* pds_empty = bias_full + 4;
     uint64_t* part_full = bias_full + 5;
     uint64_t* part_empty = part_full + NPB;
+    uint64_t* sdp_free = part_empty + NPB; // S and dP of the current step read out of TMEM
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + C::kOffAbort);
     uint8_t* keep_all = smem + C::kOffKeep;
@@ -136,7 +139,7 @@ __global__ void __launch_bounds__(320, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NST; ++s) {
-            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_full[s], 2); // TMA transaction arrival + mask operand arrival
             mbar_init(&kv_empty[s], 1 + 8);
         }
         mbar_init(bias_full, 1);
@@ -148,6 +151,7 @@ __global__ void __launch_bounds__(320, 1)
             mbar_init(&part_full[b], 1);
             mbar_init(&part_empty[b], 8);
         }
+        mbar_init(sdp_free, 8);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -219,23 +223,37 @@ __global__ void __launch_bounds__(320, 1)
             }
             for (int b = b_lo; b < b_hi; ++b, ++g) {
                 const int s = g % NST;
+                // key-mask codes of this batch row, read before waiting for the stage so the
+                // global-load latency overlaps the wait: 2 = keep, 1 = masked, 0 = past Sk
+                uint8_t codes[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int j = j0 + lane * 4 + r;
+                    codes[r] = j >= p.Sk ? 0 : (p.kmask[static_cast<int64_t>(b) * p.Sk + j] ? 2 : 1);
+                }
                 if (g >= NST && !mbar_wait(&kv_empty[s], ((g / NST) - 1) & 1, abort_flag)) {
                     goto done;
                 }
                 uint8_t* stage = smem + C::kOffStages + s * C::kStageBytes;
+                if (lane == 0) {
+                    // operand tiles first: their latency is the longest on this path
+                    mbar_arrive_expect_tx(&kv_full[s], 4 * G::kTileBytes);
+                    const int bh = b * p.H + h;
+                    tma_load_3d(stage + C::kOffSQ, &tm_q, &kv_full[s], 0, i0, bh);
+                    tma_load_3d(stage + C::kOffSdO, &tm_do, &kv_full[s], 0, i0, bh);
+                    tma_load_3d(stage + C::kOffSK, &tm_k, &kv_full[s], 0, j0, bh);
+                    tma_load_3d(stage + C::kOffSV, &tm_v, &kv_full[s], 0, j0, bh);
+                }
                 uint16_t* mo = reinterpret_cast<uint16_t*>(stage + C::kOffSMask);
                 uint8_t* keep = keep_all + s * 128;
                 bool any_excluded = false;
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     const int jj = lane * 4 + r;
-                    const int j = j0 + jj;
-                    const uint8_t code =
-                        j >= p.Sk ? 0 : (p.kmask[static_cast<int64_t>(b) * p.Sk + j] ? 2 : 1);
-                    keep[jj] = code;
-                    mo[jj * 8] = (code == 2 || p.mask_bits == 0) ? uint16_t(0)
-                                                                 : uint16_t(p.mask_bits);
-                    any_excluded |= (code != 2);
+                    keep[jj] = codes[r];
+                    mo[jj * 8] = (codes[r] == 2 || p.mask_bits == 0) ? uint16_t(0)
+                                                                     : uint16_t(p.mask_bits);
+                    any_excluded |= (codes[r] != 2);
                 }
                 const uint32_t anyx = __any_sync(0xffffffffu, any_excluded);
                 if (lane == 0) {
@@ -244,12 +262,7 @@ __global__ void __launch_bounds__(320, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&kv_full[s], 4 * G::kTileBytes);
-                    const int bh = b * p.H + h;
-                    tma_load_3d(stage + C::kOffSQ, &tm_q, &kv_full[s], 0, i0, bh);
-                    tma_load_3d(stage + C::kOffSdO, &tm_do, &kv_full[s], 0, i0, bh);
-                    tma_load_3d(stage + C::kOffSK, &tm_k, &kv_full[s], 0, j0, bh);
-                    tma_load_3d(stage + C::kOffSV, &tm_v, &kv_full[s], 0, j0, bh);
+                    mbar_arrive(&kv_full[s]); // mask operand, keep codes and flag written
                 }
                 __syncwarp();
             }
@@ -316,7 +329,7 @@ __global__ void __launch_bounds__(320, 1)
                 if (!mbar_wait(&kv_full[s], (g / NST) & 1, abort_flag)) {
                     goto done;
                 }
-                if (NST > 1 && g > 0 && !mbar_wait(pds_full, (g - 1) & 1, abort_flag)) {
+                if (NST > 1 && g > 0 && !mbar_wait(sdp_free, (g - 1) & 1, abort_flag)) {
                     goto done;
                 }
                 tc_fence_after();
@@ -334,7 +347,8 @@ __global__ void __launch_bounds__(320, 1)
                             G::kmajor(st + C::kOffSV, ks), kIdS, ks > 0);
                 }
                 umma_commit(sdp_full);
-                if (NST > 1 && g > 0 && !issue_partials(g - 1)) {
+                if (NST > 1 && g > 0 &&
+                    (!mbar_wait(pds_full, (g - 1) & 1, abort_flag) || !issue_partials(g - 1))) {
                     goto done;
                 }
             }
@@ -392,10 +406,9 @@ __global__ void __launch_bounds__(320, 1)
                         tmem_ld32(part + t * G::kDp + w * kHalf, raw);
                     }
                     tmem_ld_wait();
-                    const float f = (t == 0) ? 1.f : scale; // dK, dQ carry the scale
 #pragma unroll
                     for (int k = 0; k < kHalf; ++k) {
-                        v[k] = __uint_as_float(raw[k]) * f;
+                        v[k] = __uint_as_float(raw[k]); // dK, dQ: dS already carries the scale
                     }
                 }
                 if (w * kHalf < D) {
@@ -474,6 +487,14 @@ __global__ void __launch_bounds__(320, 1)
                 const bool select = flag_all[s] != 0 && (always_select || lse < kMaskedLogit + 104.f);
                 const float p_masked = ex2((kMaskedLogit - lse) * kLog2e);
                 const uint8_t* keep = keep_all + s * 128 + 64 * w;
+                // dS is computed pre-multiplied by the softmax scale (both dK and dQ carry it);
+                // dbias divides it out once when the tile is written.
+                const float sdelta = scale * delta;
+                // kSel: some row of this warp needs the exact masked-logit replacement (rows
+                // whose every unmasked logit is below the mask constant, or masks with no bias
+                // code); the common path carries no per-element select.
+                auto ds_tile = [&](auto sel_tag) -> bool {
+                constexpr bool kSel = decltype(sel_tag)::value;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const int col0 = 64 * w + 16 * c; // key column within the tile
@@ -481,6 +502,15 @@ __global__ void __launch_bounds__(320, 1)
                     tmem_ld16(tmem + lane_off + C::kSCol + col0, sv);
                     tmem_ld16(tmem + lane_off + C::kDPCol + col0, dpv);
                     tmem_ld_wait();
+                    if (c == 3 && NST > 1) {
+                        // S and dP are in registers: the MMA may overwrite them with the next
+                        // batch row's tiles
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) {
+                            mbar_arrive(sdp_free);
+                        }
+                    }
                     float bvals[16];
                     if constexpr (kBiasTma) {
 #pragma unroll
@@ -506,7 +536,7 @@ __global__ void __launch_bounds__(320, 1)
                     const float2 scale2 = make_float2(scale, scale);
                     const float2 l2 = make_float2(kLog2e, kLog2e);
                     const float2 nlse2 = make_float2(-lseL, -lseL);
-                    const float2 ndelta2 = make_float2(-delta, -delta);
+                    const float2 nsdelta2 = make_float2(-sdelta, -sdelta);
 #pragma unroll
                     for (int k = 0; k < 16; k += 2) {
                         const float2 t2 = ffma2(make_float2(__uint_as_float(sv[k]),
@@ -514,11 +544,11 @@ __global__ void __launch_bounds__(320, 1)
                                                 scale2, make_float2(bvals[k], bvals[k + 1]));
                         const float2 a2 = ffma2(t2, l2, nlse2);
                         float2 p2 = make_float2(ex2(a2.x), ex2(a2.y));
-                        const float2 d2 = fadd2(make_float2(__uint_as_float(dpv[k]),
+                        const float2 d2 = ffma2(make_float2(__uint_as_float(dpv[k]),
                                                             __uint_as_float(dpv[k + 1])),
-                                                ndelta2);
+                                                scale2, nsdelta2);
                         float2 ds2 = fmul2(p2, d2);
-                        if (select) {
+                        if (kSel && select) {
                             const uint8_t c0 = keep[16 * c + k], c1 = keep[16 * c + k + 1];
                             if (c0 != 2) {
                                 p2.x = (c0 == 1) ? p_masked : 0.f;
@@ -539,7 +569,7 @@ __global__ void __launch_bounds__(320, 1)
                     if (c == 0 && g > 0) {
                         // the previous step's partial-sum MMAs must be done reading P and dS
                         if (!mbar_wait(pds_empty, (g - 1) & 1, abort_flag)) {
-                            goto done;
+                            return false;
                         }
                     }
                     // 16 columns = chunks 2c, 2c+1 of this warpgroup's panel row
@@ -549,6 +579,14 @@ __global__ void __launch_bounds__(320, 1)
                         sts128(p_s + off, make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]));
                         sts128(ds_s + off, make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]));
                     }
+                }
+                return true;
+                };
+                const bool ok = __any_sync(0xffffffffu, select)
+                                    ? ds_tile(std::integral_constant<bool, true>())
+                                    : ds_tile(std::integral_constant<bool, false>());
+                if (!ok) {
+                    goto done;
                 }
                 tc_fence_before();
                 fence_proxy_async_smem();
@@ -569,8 +607,13 @@ __global__ void __launch_bounds__(320, 1)
             if (lane == 0) {
                 mbar_arrive(bias_empty);
             }
-            // dbias tile: row `row`, key columns [j0 + 64w, +64)
+            // dbias tile: row `row`, key columns [j0 + 64w, +64); the sums are of scale * dS
             if (row_ok) {
+                const float inv_scale = 1.f / scale;
+#pragma unroll
+                for (int k = 0; k < 64; ++k) {
+                    dbias[k] *= inv_scale;
+                }
                 float* dst = p.dbias + (static_cast<int64_t>(h) * p.Sq + row) * p.Sk + j0 + 64 * w;
                 const int ncol = min(64, p.Sk - (j0 + 64 * w));
                 if (p.dbias_atomic) {
