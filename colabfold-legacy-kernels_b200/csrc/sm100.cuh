@@ -95,6 +95,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     }
 }
 
+// mbar_wait by every lane of a converged warp, with a warp-uniform result (a lane that gave up
+// makes the whole warp give up), so the warp stays converged for elect.sync issue.
+__device__ __forceinline__ bool mbar_wait_w(uint64_t* bar, uint32_t parity,
+                                            volatile uint32_t* abort) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort));
+}
+
 // The same operations on a 32-bit shared-memory address (one register instead of a 64-bit
 // generic pointer; used where register pressure matters).
 __device__ __forceinline__ void mbar_arrive_s(uint32_t bar) {
@@ -175,6 +182,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
                  " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
                  "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+// Untiled bulk copy of `bytes` from global into this CTA's shared memory, completing as
+// transaction bytes on the mbarrier.  Both addresses 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
 
@@ -295,6 +312,47 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
         : "memory");
 }
 
+// Warp-converged forms: called by all 32 lanes of a converged warp; one lane, chosen by
+// elect.sync, issues.  A stream of tcgen05.mma issued this way runs at the tensor pipe's rate
+// (an N = 128 MMA every 64 cycles on B200); the same stream issued by one lane of a diverged
+// warp measured 140-220 cycles per instruction.  The elected lane is the same on every call
+// of a converged warp, so commits track the MMAs of the issuing lane.
+__device__ __forceinline__ void umma_ss_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred e, p;\n\t"
+                 "elect.sync _|e, 0xffffffff;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+__device__ __forceinline__ void umma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred e, p;\n\t"
+                 "elect.sync _|e, 0xffffffff;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_w(uint64_t* bar) {
+    asm volatile("{\n\t.reg .pred e;\n\t"
+                 "elect.sync _|e, 0xffffffff;\n\t"
+                 "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 "\n\t}" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// True on one lane of a converged warp (elect.sync).
+__device__ __forceinline__ bool elect_one() {
+    uint32_t e;
+    asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(e));
+    return e != 0;
+}
+
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -344,6 +402,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
                    "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
                    "=r"(r[30]), "=r"(r[31])
                  : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&r)[4]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3])
+                 : "memory");
 }
 
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
