@@ -175,18 +175,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == kMmaWarp) {
-        if (lane == 0) {
+        // whole warp, converged: MMAs and commits are elect.sync-issued
+        {
             constexpr uint32_t kId = idesc_f16(128, 128, false, true, E::kBf16);
             constexpr uint32_t kIdBias = idesc_f16(128, 128, false, true, E::kBf16);
             const uint64_t ones = attn::interleave16_kmajor(sbase + L.off_ones);
             const int ksteps = K / 16;
-            if (!mbar_wait(w_full, 0, abort_flag)) {
+            if (!mbar_wait_w(w_full, 0, abort_flag)) {
                 goto done;
             }
             uint32_t chunk_ctr = 0;
             for (int i = 0; i < n_mine; ++i) {
                 const int s = i & 1;
-                if (!mbar_wait(&x_full[s], (i >> 1) & 1, abort_flag)) {
+                if (!mbar_wait_w(&x_full[s], (i >> 1) & 1, abort_flag)) {
                     goto done;
                 }
                 tc_fence_after();
@@ -194,25 +195,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = 0; c < n_chunks; ++c, ++chunk_ctr) {
                     const int bf = chunk_ctr & 1;
                     if (chunk_ctr >= 2 &&
-                        !mbar_wait(&acc_empty[bf], ((chunk_ctr >> 1) - 1) & 1, abort_flag)) {
+                        !mbar_wait_w(&acc_empty[bf], ((chunk_ctr >> 1) - 1) & 1, abort_flag)) {
                         goto done;
                     }
                     tc_fence_after();
                     const uint32_t accp = tmem + bf * 256;
                     const uint32_t accg = accp + 128;
                     for (int ks = 0; ks < ksteps; ++ks) {
-                        umma_ss(accp, x_desc(x, ks), w_desc(sbase + L.off_wp, L.kb, c, ks), kId,
+                        umma_ss_w(accp, x_desc(x, ks), w_desc(sbase + L.off_wp, L.kb, c, ks), kId,
                                 ks > 0);
                     }
-                    umma_ss(accp, ones, brow_desc(sbase + L.off_bp, c), kIdBias, 1);
+                    umma_ss_w(accp, ones, brow_desc(sbase + L.off_bp, c), kIdBias, 1);
                     for (int ks = 0; ks < ksteps; ++ks) {
-                        umma_ss(accg, x_desc(x, ks), w_desc(sbase + L.off_wg, L.kb, c, ks), kId,
+                        umma_ss_w(accg, x_desc(x, ks), w_desc(sbase + L.off_wg, L.kb, c, ks), kId,
                                 ks > 0);
                     }
-                    umma_ss(accg, ones, brow_desc(sbase + L.off_bg, c), kIdBias, 1);
-                    umma_commit(&acc_full[bf]);
+                    umma_ss_w(accg, ones, brow_desc(sbase + L.off_bg, c), kIdBias, 1);
+                    umma_commit_w(&acc_full[bf]);
                 }
-                umma_commit(&x_empty[s]);
+                umma_commit_w(&x_empty[s]);
             }
         }
     } else {
@@ -511,36 +512,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == kMmaWarp) {
-        if (lane == 0) {
+        // whole warp, converged: MMAs and commits are elect.sync-issued
+        {
             constexpr uint32_t kIdRec = idesc_f16(128, 128, false, true, E::kBf16);
             const uint32_t kIdDx = idesc_f16(128, K, false, false, E::kBf16);
             const uint64_t ones = attn::interleave16_kmajor(sbase + L.ones);
             const int ksteps = K / 16;
             uint32_t cc = 0;
             for (int i = 0; i < n_mine; ++i) {
-                if (!mbar_wait(x_full, i & 1, abort_flag)) {
+                if (!mbar_wait_w(x_full, i & 1, abort_flag)) {
                     goto done;
                 }
                 for (int c = 0; c < n_chunks; ++c, ++cc) {
-                    if (!mbar_wait(chunk_full, cc & 1, abort_flag)) {
+                    if (!mbar_wait_w(chunk_full, cc & 1, abort_flag)) {
                         goto done;
                     }
                     tc_fence_after();
                     for (int ks = 0; ks < ksteps; ++ks) {
-                        umma_ss(tmem, x_desc(sbase + L.x, ks), w_desc(sbase + L.wp, K, 0, ks),
+                        umma_ss_w(tmem, x_desc(sbase + L.x, ks), w_desc(sbase + L.wp, K, 0, ks),
                                 kIdRec, ks > 0);
                     }
-                    umma_ss(tmem, ones, brow_desc(sbase + L.bp, 0), kIdRec, 1);
+                    umma_ss_w(tmem, ones, brow_desc(sbase + L.bp, 0), kIdRec, 1);
                     for (int ks = 0; ks < ksteps; ++ks) {
-                        umma_ss(tmem + 128, x_desc(sbase + L.x, ks),
+                        umma_ss_w(tmem + 128, x_desc(sbase + L.x, ks),
                                 w_desc(sbase + L.wg, K, 0, ks), kIdRec, ks > 0);
                     }
-                    umma_ss(tmem + 128, ones, brow_desc(sbase + L.bg, 0), kIdRec, 1);
-                    umma_commit(rec_full);
-                    if (!mbar_wait(ds_full, cc & 1, abort_flag)) {
+                    umma_ss_w(tmem + 128, ones, brow_desc(sbase + L.bg, 0), kIdRec, 1);
+                    umma_commit_w(rec_full);
+                    if (!mbar_wait_w(ds_full, cc & 1, abort_flag)) {
                         goto done;
                     }
-                    if (c == 0 && i > 0 && !mbar_wait(dx_drained, (i - 1) & 1, abort_flag)) {
+                    if (c == 0 && i > 0 && !mbar_wait_w(dx_drained, (i - 1) & 1, abort_flag)) {
                         goto done;
                     }
                     tc_fence_after();
@@ -548,16 +550,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks) {
                         const uint32_t boff = (ks >> 2) * (K * 128) + (ks & 3) * 32;
-                        umma_ss(tmem + 256, x_desc(sbase + L.dp, ks),
+                        umma_ss_w(tmem + 256, x_desc(sbase + L.dp, ks),
                                 smem_desc(sbase + L.wp + boff, 16, 1024, kSwizzle128), kIdDx,
                                 (c > 0 || ks > 0) ? 1u : 0u);
-                        umma_ss(tmem + 256, x_desc(sbase + L.dg, ks),
+                        umma_ss_w(tmem + 256, x_desc(sbase + L.dg, ks),
                                 smem_desc(sbase + L.wg + boff, 16, 1024, kSwizzle128), kIdDx, 1);
                     }
-                    umma_commit(dx_done);
+                    umma_commit_w(dx_done);
                 }
-                umma_commit(tile_done);
-                umma_commit(dx_full);
+                umma_commit_w(tile_done);
+                umma_commit_w(dx_full);
             }
         }
     } else {
@@ -803,12 +805,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == kMmaWarp) {
-        if (lane == 0) {
+        // whole warp, converged: MMAs and commits are elect.sync-issued
+        {
             constexpr uint32_t kIdRec = idesc_f16(128, 64, false, true, E::kBf16);
             constexpr uint32_t kIdDw = idesc_f16(128, 64, true, true, E::kBf16);
             const uint64_t ones = attn::interleave16_kmajor(sbase + L.ones);
             const int ksteps = K / 16;
-            if (!mbar_wait(w_full, 0, abort_flag)) {
+            if (!mbar_wait_w(w_full, 0, abort_flag)) {
                 goto done;
             }
             auto issue_dw = [&](int i) {
@@ -818,22 +821,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int ks = 0; ks < 8; ++ks) {
                     const uint64_t a = smem_desc(xs + ks * 2048, 16384, 1024, kSwizzle128);
                     const uint32_t acc = (i > 0 || ks > 0) ? 1u : 0u;
-                    umma_ss(tmem + 128, a, smem_desc(sbase + L.hi_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
-                    umma_ss(tmem + 128, a, smem_desc(sbase + L.lo_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
-                    umma_ss(tmem + 192, a, smem_desc(sbase + L.hi_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
-                    umma_ss(tmem + 192, a, smem_desc(sbase + L.lo_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
+                    umma_ss_w(tmem + 128, a, smem_desc(sbase + L.hi_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
+                    umma_ss_w(tmem + 128, a, smem_desc(sbase + L.lo_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
+                    umma_ss_w(tmem + 192, a, smem_desc(sbase + L.hi_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
+                    umma_ss_w(tmem + 192, a, smem_desc(sbase + L.lo_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
                 }
-                umma_commit(dw_done);
-                umma_commit(&in_empty[i & 1]);
+                umma_commit_w(dw_done);
+                umma_commit_w(&in_empty[i & 1]);
             };
             for (int i = 0; i < n_mine; ++i) {
                 const int s = i & 1;
-                if (!mbar_wait(&in_full[s], (i >> 1) & 1, abort_flag)) {
+                if (!mbar_wait_w(&in_full[s], (i >> 1) & 1, abort_flag)) {
                     goto done;
                 }
                 if (i > 0) {
                     // tensor memory p, g is free once the epilogue has read tile i-1
-                    if (!mbar_wait(ds_full, (i - 1) & 1, abort_flag)) {
+                    if (!mbar_wait_w(ds_full, (i - 1) & 1, abort_flag)) {
                         goto done;
                     }
                     tc_fence_after();
@@ -841,17 +844,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const uint32_t xs = sbase + L.x + s * 32768;
                 for (int ks = 0; ks < ksteps; ++ks) {
-                    umma_ss(tmem, x_desc(xs, ks), smem_desc(sbase + L.wp + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
+                    umma_ss_w(tmem, x_desc(xs, ks), smem_desc(sbase + L.wp + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
                 }
-                umma_ss(tmem, ones, smem_desc(sbase + L.bp, 128, 256, kInterleave), kIdRec, 1);
+                umma_ss_w(tmem, ones, smem_desc(sbase + L.bp, 128, 256, kInterleave), kIdRec, 1);
                 for (int ks = 0; ks < ksteps; ++ks) {
-                    umma_ss(tmem + 64, x_desc(xs, ks), smem_desc(sbase + L.wg + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
+                    umma_ss_w(tmem + 64, x_desc(xs, ks), smem_desc(sbase + L.wg + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
                 }
-                umma_ss(tmem + 64, ones, smem_desc(sbase + L.bg, 128, 256, kInterleave), kIdRec, 1);
-                umma_commit(rec_full);
+                umma_ss_w(tmem + 64, ones, smem_desc(sbase + L.bg, 128, 256, kInterleave), kIdRec, 1);
+                umma_commit_w(rec_full);
             }
             if (n_mine > 0) {
-                if (!mbar_wait(ds_full, (n_mine - 1) & 1, abort_flag)) {
+                if (!mbar_wait_w(ds_full, (n_mine - 1) & 1, abort_flag)) {
                     goto done;
                 }
                 tc_fence_after();

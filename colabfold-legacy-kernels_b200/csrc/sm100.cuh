@@ -152,6 +152,11 @@ __device__ __forceinline__ bool mbar_wait_s(uint32_t bar, uint32_t parity, uint3
     return mbar_wait_slow_s(bar, parity, abort);
 }
 
+// mbar_wait_s by every lane of a converged warp, with a warp-uniform result.
+__device__ __forceinline__ bool mbar_wait_s_w(uint32_t bar, uint32_t parity, uint32_t abort) {
+    return __all_sync(0xffffffffu, mbar_wait_s(bar, parity, abort));
+}
+
 // ---------------------------------------------------------------------------------------------
 // Proxy fences
 // ---------------------------------------------------------------------------------------------
