@@ -340,7 +340,8 @@ def run_ours(args, rank, world, local_rank):
         "flops_per_launch": bwd_flops_launch,
         "ms_per_launch": ms_bwd,
         "fwd_kernel": {"achieved": 4 * n * HEADS * N_RES * N_RES * HEAD_DIM / (ms_fwd * 1e-3) / 1e12,
-                       "ms_per_launch": ms_fwd, "unit": "TFLOP/s"},
+                       "ms_per_launch": ms_fwd, "unit": "TFLOP/s",
+                       "traffic": traffic_from_profiles("attn_fwd_tri768")},
     }
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -359,7 +360,71 @@ def run_ours(args, rank, world, local_rank):
     }
     if world == 1 and not args.skip_extras:
         result["layernorm"] = bench_layernorm(dev, pk)
+        result["gdp"] = bench_gdp(dev, pk)
     return result
+
+
+def _median_ms(fn, steps, flush=None):
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        fn()
+    ts = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()  # untimed: evicts L2
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
+
+
+def bench_gdp(dev, pk, steps=20):
+    """Gated dual projection forward and backward on config C4 (M = 1024*1024, K = 128, the
+    a/b pair as one call with N = 256, bf16).  Roofline: the larger of bytes / measured HBM
+    bandwidth and flops / measured dense bf16 peak (burst), divided by the measured time."""
+    import torch
+    import oracle
+    from colabfold_legacy_kernels import torch_ops
+    inp = oracle.configs.make_ln_gdp_inputs(oracle.configs.C4, device=dev)
+    x, wp, bp, wg, bg, mask, dout = (inp[k] for k in ("x", "wp", "bp", "wg", "bg", "mask", "dout"))
+    m, kk = x.shape
+    n = wp.shape[1]
+    out = torch.empty((m, n), dtype=x.dtype, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    res = {}
+
+    def line(name, ms, flops, nbytes, traffic):
+        t_bound = max(nbytes / (pk["hbm_gbs"] * 1e9), flops / (pk["bf16"] * 1e12))
+        return {"metric": "GDP %s TFLOP/s [1M x 128 -> 256] bf16" % name,
+                "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
+                "hbm_gbs": nbytes / (ms * 1e-3) / 1e9,
+                "roofline": {"bound": "hbm" if nbytes / pk["hbm_gbs"] / 1e9 >= flops / pk["bf16"] / 1e12
+                             else "tensor", "algorithmic_bytes": nbytes, "flops": flops,
+                             "bound_ms": t_bound * 1e3, "frac": t_bound * 1e3 / ms,
+                             "traffic": traffic,
+                             "peaks": {"hbm_gbs": pk["hbm_gbs"], "bf16_tflops": pk["bf16"]}}}
+
+    ms = _median_ms(lambda: torch_ops.gdp_fwd(x, wp, bp, wg, bg, mask, out=out), steps, flush)
+    fwd_bytes = 2 * (m * kk + m * n + m + 2 * kk * n + 2 * n)
+    res["fwd"] = line("fwd", ms, oracle.gdp.flops_fwd(m, kk, n), fwd_bytes,
+                      traffic_from_profiles("gdp_fwd_c4"))
+    nbytes = cabi_gdp_workspace(m, kk, n)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+    ms = _median_ms(lambda: torch_ops.gdp_bwd(x, wp, bp, wg, bg, mask, dout, workspace=ws),
+                    steps, flush)
+    bwd_bytes = 2 * (m * kk + m * n + m * kk + m) + 4 * (2 * kk * n + 2 * n)
+    dx_t, dw_t = traffic_from_profiles("gdp_bwd_dx_c4"), traffic_from_profiles("gdp_bwd_dw_c4")
+    res["bwd"] = line("bwd", ms, oracle.gdp.flops_bwd(m, kk, n), bwd_bytes,
+                      dx_t + dw_t if dx_t and dw_t else None)
+    return res
+
+
+def cabi_gdp_workspace(m, k, n):
+    from colabfold_legacy_kernels import cabi
+    return cabi.workspace_size("cfk_gdp_bwd_workspace_size", m, k, n)
 
 
 def bench_layernorm(dev, pk, steps=20):
@@ -406,7 +471,8 @@ def bench_layernorm(dev, pk, steps=20):
     res["bwd"] = {"metric": "LayerNorm bwd HBM GB/s [1M x 128] bf16", "value": gbs,
                   "unit": "GB/s", "ms": ms, "roofline": {"bound": "hbm", "achieved": gbs,
                                                          "peak": pk["hbm_gbs"], "unit": "GB/s",
-                                                         "frac": gbs / pk["hbm_gbs"]}}
+                                                         "frac": gbs / pk["hbm_gbs"],
+                                                         "traffic": traffic_from_profiles("ln_bwd_c4")}}
     return res
 
 
@@ -425,8 +491,17 @@ def main():
                     help="profiling only: attention rows on this GPU instead of 768/N")
     ap.add_argument("--profile", action="store_true",
                     help="profiling only: time the attention steps and stop (no e2e/extras/cpu)")
+    ap.add_argument("--profile-extras", action="store_true",
+                    help="profiling only: run the LayerNorm and GDP lines (C4) alone, 2 steps")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.profile_extras:
+        import torch
+        dev = torch.device("cuda", 0)
+        pk = peaks()
+        print(json.dumps({"profile": True, "layernorm": bench_layernorm(dev, pk, steps=2),
+                          "gdp": bench_gdp(dev, pk, steps=2)}), flush=True)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -451,9 +526,9 @@ def main():
         res = run_ours(args, rank, world, local_rank)
         if rank == 0 and world == 1 and not args.skip_cpu and not args.profile:
             # size the sample to ~5 s per repetition (3 repetitions, ~15 s of CPU work)
-            probe = cpu_sample_inputs(8)
-            t8, _, _ = cpu_attention_sample(probe, 8)
-            rows = int(max(8, min(N_RES, 8 * 5.0 / max(t8, 1e-3))))
+            probe = cpu_sample_inputs(32)
+            t32, _, _ = cpu_attention_sample(probe, 32)
+            rows = int(max(8, min(N_RES, 32 * 5.0 / max(t32, 1e-3))))
             inputs = cpu_sample_inputs(rows)
             sec, flops, threads = cpu_attention_sample(inputs, rows, reps=3)
             res["cpu_baseline"] = {
