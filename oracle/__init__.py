@@ -19,9 +19,8 @@ include/cfk.h and colabfold_legacy_kernels) never calls it and has no CPU fallba
 Parity pin: the reference ships no tests, golden vectors or fixtures for this path.  The
 forward restatements are pinned against outputs of the reference's own kernels, compiled from
 its sources for sm_100a by oracle/legacy_ref/ and run on a B200; the vectors live in
-tests/golden/ (see tests/golden/make_golden.py).  Until those vectors exist in a checkout the
-forward parity is unpinned; the backward has no reference counterpart and is pinned to
-torch.autograd of the pinned forward.
+tests/golden/ (made by tests/golden/make_golden.py, checked by tests/test_golden.py).  The
+backward has no reference counterpart and is pinned to torch.autograd of the pinned forward.
 """
 
 from .attention import (MASKED_LOGIT, attention_bwd, attention_fwd, attention_logits,
