@@ -69,18 +69,53 @@ def traffic_from_profiles(key):
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons in the background."""
+    """Samples the SM clock and the clock-event (throttle) reasons of one GPU in a background
+    thread while the timed region runs: NVML every ~2 ms (timed regions can be a few tens of
+    ms), or nvidia-smi every 50 ms when NVML is unavailable.  Read-only."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, index):
+    def __init__(self, index, device=None):
         self.index = index
+        self.device = device
         self.proc = None
+        self.nvml = None
         self.lines = []
+        self.samples = []  # (sm_mhz, reason bits)
+        self.max_mhz = None
+        self.stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        handle = None
+        try:
+            import torch
+            p = torch.cuda.get_device_properties(self.device if self.device is not None
+                                                 else self.index)
+            bus = "%08X:%02X:%02X.0" % (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        return pynvml, handle
 
     def __enter__(self):
+        try:
+            pynvml, h = self._nvml_handle()
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.nvml = (pynvml, h, reasons)
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
@@ -92,11 +127,24 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll_nvml(self):
+        pynvml, h, reasons = self.nvml
+        while not self.stop.is_set():
+            try:
+                self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                                     int(reasons(h))))
+            except Exception:
+                return
+            time.sleep(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.nvml:
+            self.thread.join(timeout=2)
         if self.proc:
             self.proc.terminate()
             try:
@@ -106,7 +154,12 @@ class ClockSampler:
             self.thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons = [], self.max_mhz, set()
+        for mhz, bits in self.samples:
+            sm.append(mhz)
+            for name, bit in self.REASON_BITS.items():
+                if bits & bit:
+                    reasons.add(name)
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
             parts = [x.strip() for x in line.split(",")]
@@ -121,9 +174,9 @@ class ClockSampler:
                 if val.lower() == "active":
                     reasons.add(name)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvml" if self.samples else "nvidia-smi"}
 
 
 # ------------------------------------------------------------------------------------------
@@ -260,7 +313,7 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.barrier()
     step_ms, fwd_ms, bwd_ms = [], [], []
-    with ClockSampler(local_rank) as clocks:
+    with ClockSampler(local_rank, dev) as clocks:
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
