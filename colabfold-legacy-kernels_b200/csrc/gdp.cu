@@ -50,7 +50,8 @@ struct FwdLayout {
     int kb;        // K (multiple of 16, <= 128)
     int npad;      // N rounded up to 128
     int x_stage;   // one x tile: ceil(K/64) panels of 128 rows x 128 B
-    int off_x, off_wp, off_wg, off_bp, off_bg, off_ones, off_bar, total;
+    int xs;        // x stages (2 when they fit beside the weights, else 1)
+    int off_x, off_wp, off_wg, off_bp, off_bg, off_ones, off_stg, off_bar, total;
 };
 
 __host__ __device__ inline FwdLayout fwd_layout(int K, int N) {
@@ -58,14 +59,20 @@ __host__ __device__ inline FwdLayout fwd_layout(int K, int N) {
     L.kb = K;
     L.npad = (N + 127) / 128 * 128;
     L.x_stage = ((K + 63) / 64) * 16384;
-    L.off_x = 0;
-    L.off_wp = 2 * L.x_stage;
-    L.off_wg = L.off_wp + L.kb * L.npad * 2;
-    L.off_bp = L.off_wg + L.kb * L.npad * 2;
-    L.off_bg = L.off_bp + (L.npad / 8) * 256;
-    L.off_ones = L.off_bg + (L.npad / 8) * 256;
-    L.off_bar = L.off_ones + 4096;
-    L.total = L.off_bar + 16 * 8 + 16 + 1024;
+    for (L.xs = 2; L.xs >= 1; --L.xs) {
+        L.off_x = 0;
+        L.off_wp = L.xs * L.x_stage;
+        L.off_wg = L.off_wp + L.kb * L.npad * 2;
+        L.off_bp = L.off_wg + L.kb * L.npad * 2;
+        L.off_bg = L.off_bp + (L.npad / 8) * 256;
+        L.off_ones = L.off_bg + (L.npad / 8) * 256;
+        L.off_stg = L.off_ones + 4096; // output staging: one [128 x 64] box per warpgroup
+        L.off_bar = L.off_stg + 2 * 16384;
+        L.total = L.off_bar + 16 * 8 + 16 + 1024;
+        if (L.total <= 227 * 1024) {
+            break;
+        }
+    }
     return L;
 }
 
@@ -89,9 +96,10 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     gdp_fwd_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_wp,
-                   const __grid_constant__ CUtensorMap tm_wg, const uint16_t* __restrict__ bp,
-                   const uint16_t* __restrict__ bg, const uint16_t* __restrict__ mask,
-                   uint16_t* __restrict__ out, int M, int K, int N) {
+                   const __grid_constant__ CUtensorMap tm_wg,
+                   const __grid_constant__ CUtensorMap tm_out, const uint16_t* __restrict__ bp,
+                   const uint16_t* __restrict__ bg, const uint16_t* __restrict__ mask, int M,
+                   int K, int N) {
     using E = Elem<T>;
     const FwdLayout L = fwd_layout(K, N);
     extern __shared__ uint8_t smem_raw[];
@@ -163,8 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int panels = (K + 63) / 64;
             for (int i = 0; i < n_mine; ++i) {
                 const int mt = blockIdx.x + i * gridDim.x;
-                const int s = i & 1;
-                if (i >= 2 && !mbar_wait(&x_empty[s], ((i >> 1) - 1) & 1, abort_flag)) {
+                const int s = i % L.xs;
+                if (i >= L.xs && !mbar_wait(&x_empty[s], ((i / L.xs) - 1) & 1, abort_flag)) {
                     goto done;
                 }
                 mbar_arrive_expect_tx(&x_full[s], panels * 16384);
@@ -186,8 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             uint32_t chunk_ctr = 0;
             for (int i = 0; i < n_mine; ++i) {
-                const int s = i & 1;
-                if (!mbar_wait_w(&x_full[s], (i >> 1) & 1, abort_flag)) {
+                const int s = i % L.xs;
+                if (!mbar_wait_w(&x_full[s], (i / L.xs) & 1, abort_flag)) {
                     goto done;
                 }
                 tc_fence_after();
@@ -217,10 +225,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // epilogue: thread (w, r) owns row r and columns [64w, 64w + 64) of each chunk
+        // epilogue: thread (w, r) owns row r and columns [64w, 64w + 64) of each chunk; the
+        // warpgroup stages its [128 x 64] box (128-byte swizzle) in shared memory and one thread
+        // writes it with a TMA store (rows >= M and columns >= N are clipped by the map)
         const int w = warp >> 2;
         const int r = static_cast<int>(attn::warp_lane_base()) + lane;
         const uint32_t lane_off = attn::warp_lane_base() << 16;
+        const uint32_t stg_row = sbase + L.off_stg + w * 16384 + r * 128;
+        const bool leader = (threadIdx.x == 128 * w);
         uint32_t chunk_ctr = 0;
         for (int i = 0; i < n_mine; ++i) {
             const int mt = blockIdx.x + i * gridDim.x;
@@ -229,7 +241,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float hm = row_ok ? 0.5f * E::to_float(mask[row]) : 0.f;
             for (int c = 0; c < n_chunks; ++c, ++chunk_ctr) {
                 const int bf = chunk_ctr & 1;
-                if (!mbar_wait(&acc_full[bf], (chunk_ctr >> 1) & 1, abort_flag)) {
+                const bool ok = mbar_wait(&acc_full[bf], (chunk_ctr >> 1) & 1, abort_flag);
+                if (leader) {
+                    bulk_wait_read<0>(); // the previous store has read the staging box
+                }
+                named_bar_sync(1 + w, 128); // every thread arrives, also after a failed wait
+                if (!ok || *abort_flag) {
                     goto done;
                 }
                 __syncwarp();
@@ -256,25 +273,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         o[e] = E::pack(y[0], y[1]);
                     }
-                    const int n0 = c * 128 + 64 * w + 16 * q;
-                    if (row_ok && n0 < N) {
-                        uint16_t* dst = out + static_cast<int64_t>(row) * N + n0;
-                        st_global_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
-                        if (n0 + 8 < N) {
-                            st_global_v4(dst + 8, make_uint4(o[4], o[5], o[6], o[7]));
-                        }
-                    }
+                    // columns 16q..16q+15 of the box row = 16-byte chunks 2q, 2q+1
+                    attn::sts128(stg_row + (((2 * q) ^ (r & 7)) << 4),
+                                 make_uint4(o[0], o[1], o[2], o[3]));
+                    attn::sts128(stg_row + (((2 * q + 1) ^ (r & 7)) << 4),
+                                 make_uint4(o[4], o[5], o[6], o[7]));
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&acc_empty[bf]);
                 }
+                fence_proxy_async_smem();
+                named_bar_sync(1 + w, 128);
+                if (leader) {
+                    tma_store_3d(&tm_out, sbase + L.off_stg + w * 16384, c * 128 + 64 * w,
+                                 mt * 128, 0);
+                    bulk_commit();
+                }
             }
+        }
+        if (leader) {
+            bulk_wait<0>(); // stores complete before the CTA retires
         }
     }
 done:
     __syncwarp();
+    if (warp < kProducerWarp && (threadIdx.x & 127) == 0) {
+        bulk_wait<0>(); // no store may still read the staging boxes (also on the abort path)
+    }
     if (*abort_flag) {
         const unsigned long long t0 = global_ns();
         while (global_ns() - t0 < 200000ull) {
@@ -343,20 +370,22 @@ int gdp_fwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const vo
             static_cast<uint16_t*>(out), M, K, N);
         return check_launch("gdp_fwd_generic");
     }
-    CUtensorMap tx, twp, twg;
-    // x [M, K]: dims (K, M, 1), box 64 x 128; weights [K, N]: dims (N, K, 1), box 64 x K
+    CUtensorMap tx, twp, twg, tout;
+    // x [M, K]: dims (K, M, 1), box 64 x 128; weights [K, N]: dims (N, K, 1), box 64 x K;
+    // out [M, N]: dims (N, M, 1), box 64 x 128 (stores)
     CFK_TRY(make_tmap_3d(&tx, x, K, M, 1, 2ull * K, 2ull * K * M, 64, 128, 1, 128, "gdp x"));
     CFK_TRY(make_tmap_3d(&twp, wp, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wp"));
     CFK_TRY(make_tmap_3d(&twg, wg, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wg"));
+    CFK_TRY(make_tmap_3d(&tout, out, N, M, 1, 2ull * N, 2ull * N * M, 64, 128, 1, 128,
+                         "gdp out"));
     auto kern = gdp_fwd_kernel<T>;
     CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
                              "gdp_fwd"));
     const int n_mt = (M + 127) / 128;
     const int grid = std::min(n_mt, dev.num_sms);
-    kern<<<grid, kThreads, L.total, st>>>(tx, twp, twg, static_cast<const uint16_t*>(bp),
+    kern<<<grid, kThreads, L.total, st>>>(tx, twp, twg, tout, static_cast<const uint16_t*>(bp),
                                           static_cast<const uint16_t*>(bg),
-                                          static_cast<const uint16_t*>(mask),
-                                          static_cast<uint16_t*>(out), M, K, N);
+                                          static_cast<const uint16_t*>(mask), M, K, N);
     return check_launch("gdp_fwd");
 }
 

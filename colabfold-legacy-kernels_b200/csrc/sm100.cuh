@@ -203,6 +203,17 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 // Tiled add-reduction of a shared-memory box into global memory through a tensor map (f32 map:
 // element-wise f32 add, performed at L2).  Completes through the issuing thread's bulk group.
 // Out-of-range parts of the box are skipped.  Coordinates must not be negative.
+// Tiled store of a shared-memory box into global memory through a tensor map, completed through
+// the issuing thread's bulk group.  Out-of-range parts of the box are skipped; coordinates must
+// not be negative and the innermost one times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int32_t c0,
+                                             int32_t c1, int32_t c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group"
+                 " [%0, {%2, %3, %4}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src,
                                                   int32_t c0, int32_t c1, int32_t c2) {
     asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group"
