@@ -755,9 +755,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* w_full = bars + 0;
     uint64_t* in_full = bars + 1;    // [2] x tile + dout chunk
     uint64_t* in_empty = bars + 3;   // [2]
-    uint64_t* rec_full = bars + 5;
-    uint64_t* ds_full = bars + 6;    // count 8
-    uint64_t* dw_done = bars + 7;
+    uint64_t* rec_full = bars + 5;   // [2] p, g of a tile in tensor-memory buffer i & 1
+    uint64_t* ds_full = bars + 7;    // count 8
+    uint64_t* dw_done = bars + 8;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + 16 * 8);
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(tmem_slot + 1);
     float* red = reinterpret_cast<float*>(smem + L.red);
@@ -774,8 +774,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < 2; ++s) {
             mbar_init(&in_full[s], 1);
             mbar_init(&in_empty[s], 1);
+            mbar_init(&rec_full[s], 1);
         }
-        mbar_init(rec_full, 1);
         mbar_init(ds_full, 8);
         mbar_init(dw_done, 1);
         *abort_flag = 0;
@@ -805,13 +805,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(tmem_slot, 256);
+        tmem_alloc(tmem_slot, 512);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // tensor memory: p at 0, g at 64, dwp at 128, dwg at 192
+    // tensor memory: p, g of tile i at (i & 1) * 128 + {0, 64}; dwp at 256, dwg at 320.  The
+    // two p/g buffers let the recompute of tile i+1 run while the epilogue works on tile i.
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
@@ -850,10 +851,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int ks = 0; ks < 8; ++ks) {
                     const uint64_t a = smem_desc(xs + ks * 2048, 16384, 1024, kSwizzle128);
                     const uint32_t acc = (i > 0 || ks > 0) ? 1u : 0u;
-                    umma_ss_w(tmem + 128, a, smem_desc(sbase + L.hi_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
-                    umma_ss_w(tmem + 128, a, smem_desc(sbase + L.lo_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
-                    umma_ss_w(tmem + 192, a, smem_desc(sbase + L.hi_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
-                    umma_ss_w(tmem + 192, a, smem_desc(sbase + L.lo_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
+                    umma_ss_w(tmem + 256, a, smem_desc(sbase + L.hi_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
+                    umma_ss_w(tmem + 256, a, smem_desc(sbase + L.lo_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
+                    umma_ss_w(tmem + 320, a, smem_desc(sbase + L.hi_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
+                    umma_ss_w(tmem + 320, a, smem_desc(sbase + L.lo_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
                 }
                 umma_commit_w(dw_done);
                 umma_commit_w(&in_empty[i & 1]);
@@ -863,24 +864,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait_w(&in_full[s], (i >> 1) & 1, abort_flag)) {
                     goto done;
                 }
+                // p, g of tile i into buffer i & 1: its previous user, tile i-2, was read by
+                // the epilogue before ds_full(i-2), which this loop waited for already
+                const uint32_t xs = sbase + L.x + s * 32768;
+                const uint32_t pg = tmem + s * 128;
+                for (int ks = 0; ks < ksteps; ++ks) {
+                    umma_ss_w(pg, x_desc(xs, ks), smem_desc(sbase + L.wp + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
+                }
+                umma_ss_w(pg, ones, smem_desc(sbase + L.bp, 128, 256, kInterleave), kIdRec, 1);
+                for (int ks = 0; ks < ksteps; ++ks) {
+                    umma_ss_w(pg + 64, x_desc(xs, ks), smem_desc(sbase + L.wg + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
+                }
+                umma_ss_w(pg + 64, ones, smem_desc(sbase + L.bg, 128, 256, kInterleave), kIdRec, 1);
+                umma_commit_w(&rec_full[s]);
                 if (i > 0) {
-                    // tensor memory p, g is free once the epilogue has read tile i-1
+                    // dW of tile i-1 once its epilogue has written the hi / lo tiles
                     if (!mbar_wait_w(ds_full, (i - 1) & 1, abort_flag)) {
                         goto done;
                     }
                     tc_fence_after();
                     issue_dw(i - 1);
                 }
-                const uint32_t xs = sbase + L.x + s * 32768;
-                for (int ks = 0; ks < ksteps; ++ks) {
-                    umma_ss_w(tmem, x_desc(xs, ks), smem_desc(sbase + L.wp + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
-                }
-                umma_ss_w(tmem, ones, smem_desc(sbase + L.bp, 128, 256, kInterleave), kIdRec, 1);
-                for (int ks = 0; ks < ksteps; ++ks) {
-                    umma_ss_w(tmem + 64, x_desc(xs, ks), smem_desc(sbase + L.wg + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
-                }
-                umma_ss_w(tmem + 64, ones, smem_desc(sbase + L.bg, 128, 256, kInterleave), kIdRec, 1);
-                umma_commit_w(rec_full);
             }
             if (n_mine > 0) {
                 if (!mbar_wait_w(ds_full, (n_mine - 1) & 1, abort_flag)) {
@@ -900,7 +904,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row = mt * 128 + r;
             const bool row_ok = row < M;
             const float mk = row_ok ? E::to_float(mask[row]) : 0.f;
-            if (!mbar_wait(rec_full, i & 1, abort_flag) ||
+            if (!mbar_wait(&rec_full[i & 1], (i >> 1) & 1, abort_flag) ||
                 !mbar_wait(&in_full[i & 1], (i >> 1) & 1, abort_flag)) {
                 goto done;
             }
@@ -913,8 +917,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             float vp[32], vg[32];
             {
                 uint32_t pv[32], gv[32];
-                tmem_ld32(tmem + lane_off + 32 * w, pv);
-                tmem_ld32(tmem + lane_off + 64 + 32 * w, gv);
+                const uint32_t pg = tmem + lane_off + (i & 1) * 128 + 32 * w;
+                tmem_ld32(pg, pv);
+                tmem_ld32(pg + 64, gv);
                 tmem_ld_wait();
                 const uint32_t do_row = sbase + L.dout + (i & 1) * 16384 + r * 128;
 #pragma unroll
@@ -988,8 +993,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             tc_fence_after();
             uint32_t a[32], b[32];
-            tmem_ld32(tmem + lane_off + 128 + 32 * w, a);
-            tmem_ld32(tmem + lane_off + 192 + 32 * w, b);
+            tmem_ld32(tmem + lane_off + 256 + 32 * w, a);
+            tmem_ld32(tmem + lane_off + 320 + 32 * w, b);
             tmem_ld_wait();
             if (r < K) {
 #pragma unroll
@@ -1014,7 +1019,7 @@ done:
     __syncthreads();
     tc_fence_after();
     if (warp == kMmaWarp) {
-        tmem_dealloc(tmem, 256);
+        tmem_dealloc(tmem, 512);
     }
 }
 
