@@ -42,7 +42,7 @@ __device__ __forceinline__ float sigmoid_fast(float x) {
 
 // sigmoid through exp2: f32-accurate (used by the backward, whose f32 outputs need it).
 __device__ __forceinline__ float sigmoid_accurate(float x) {
-    return 1.0f / (1.0f + ex2(-x * kLog2e));
+    return rcp_approx(1.0f + ex2(-x * kLog2e));
 }
 
 // Offsets of the forward kernel's shared memory (bytes from a 1024-aligned base).
@@ -694,6 +694,334 @@ done:
 }
 
 // ------------------------------------------------------------------------------------------
+// dx with both weight matrices resident in shared memory (the shapes whose weights fit beside
+// two x stages).  Per 128-row tile of x and per 64-column chunk j:
+//   [p | g] = x [wp_j | wg_j] + [bp_j | bg_j]   one N = 128 MMA chain: the 64-column atoms
+//                                               j of wp and of wg form the B operand
+//   dp, dg  -> the same tensor-memory columns, as packed 16-bit pairs (tcgen05.st)
+//   dx     += dp wp_j^T + dg wg_j^T             A read from tensor memory (TS form)
+// The epilogue reads dout straight from global memory (one chunk ahead in registers, the next
+// tile's lines prefetched into L2), which leaves the shared memory to the weights and x.
+// Tensor memory: [p | g] buffers at 0 and 128 (chunk counter & 1), dx buffers at 256 and 384
+// (tile counter & 1).  The chunk buffer of chunk c is rewritten by the recompute of chunk
+// c + 2, which the MMA warp issues after the dx MMAs of chunk c (tcgen05.mma runs in issue
+// order, so the dx MMAs read dp / dg before the recompute overwrites them).
+// ------------------------------------------------------------------------------------------
+struct DxrLayout {
+    int nch;    // 64-column chunks of N
+    int xpan;   // 64-column panels of an x tile
+    int xs;     // x stages
+    int w, brow, ones, x, bar, total;
+};
+
+__host__ __device__ inline DxrLayout dxr_layout(int K, int N) {
+    DxrLayout L;
+    L.nch = (N + 63) / 64;
+    L.xpan = (K + 63) / 64;
+    L.w = 0;                                   // wp atoms, then wg atoms: K x 128 B each
+    L.brow = L.w + 2 * L.nch * K * 128;        // per chunk [16 x 128] interleave: bp_j | bg_j
+    L.ones = L.brow + L.nch * 4096;
+    L.x = L.ones + 4096;
+    for (L.xs = 2; L.xs >= 1; --L.xs) {
+        L.bar = L.x + L.xs * L.xpan * 16384;
+        L.total = L.bar + 16 * 8 + 16 + 1024;
+        if (L.total <= 227 * 1024) {
+            break;
+        }
+    }
+    return L;
+}
+
+constexpr int kDxrThreads = 320; // 8 epilogue warps (2 per lane quarter), producer, MMA
+constexpr int kDxrProducer = 8;
+constexpr int kDxrMma = 9;
+constexpr int kDxrCols = 32;     // columns of a 64-column chunk per epilogue warp
+
+template <typename T>
+__global__ void __launch_bounds__(kDxrThreads, 1)
+    gdp_bwd_dxr_kernel(const __grid_constant__ CUtensorMap tm_x,
+                       const __grid_constant__ CUtensorMap tm_wp,
+                       const __grid_constant__ CUtensorMap tm_wg,
+                       const uint16_t* __restrict__ bp, const uint16_t* __restrict__ bg,
+                       const uint16_t* __restrict__ mask, const uint16_t* __restrict__ dout,
+                       uint16_t* __restrict__ dx, int M, int K, int N) {
+    using E = Elem<T>;
+    const DxrLayout L = dxr_layout(K, N);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t sbase = smem_u32(smem);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar);
+    uint64_t* w_full = bars + 0;     // weights loaded
+    uint64_t* x_full = bars + 1;     // [2]
+    uint64_t* x_empty = bars + 3;    // [2] recompute MMAs of the tile done
+    uint64_t* pg_full = bars + 5;    // [2] p, g of a chunk in tensor memory
+    uint64_t* ds_full = bars + 7;    // [2] dp, dg of a chunk in tensor memory (count 8)
+    uint64_t* dx_full = bars + 9;    // [2] dx of a tile complete
+    uint64_t* dx_empty = bars + 11;  // [2] dx of a tile read out (count 8)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + 16 * 8);
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n_mt = (M + 127) / 128;
+    const int nch = L.nch;
+    const int n_mine = (n_mt - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                       static_cast<int>(gridDim.x);
+
+    if (threadIdx.x == 0) {
+        mbar_init(w_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&x_full[s], 1);
+            mbar_init(&x_empty[s], 1);
+            mbar_init(&pg_full[s], 1);
+            mbar_init(&ds_full[s], 8);
+            mbar_init(&dx_full[s], 1);
+            mbar_init(&dx_empty[s], 8);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    {
+        const uint32_t one = E::kBf16 ? 0x3F80u : 0x3C00u;
+        uint32_t* ones = reinterpret_cast<uint32_t*>(smem + L.ones);
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+            ones[i] = ((i < 512) && ((i & 3) == 0)) ? one : 0u;
+        }
+        // bias rows: chunk j holds bp[64j, 64j + 64) in columns 0..63, bg in 64..127
+        for (int j = warp; j < nch; j += kDxrThreads / 32) {
+            uint16_t* b = reinterpret_cast<uint16_t*>(smem + L.brow + j * 4096);
+            build_brow(b, bp, 64 * j, 64, N, lane);
+            build_brow(b + 1024, bg, 64 * j, 64, N, lane);
+        }
+        fence_proxy_async_smem();
+    }
+    if (warp == kDxrMma) {
+        tmem_alloc(tmem_slot, 512);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kDxrProducer) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(w_full, 2 * nch * K * 128);
+            for (int j = 0; j < nch; ++j) {
+                tma_load_3d(smem + L.w + j * K * 128, &tm_wp, w_full, 64 * j, 0, 0);
+                tma_load_3d(smem + L.w + (nch + j) * K * 128, &tm_wg, w_full, 64 * j, 0, 0);
+            }
+            for (int t = 0; t < n_mine; ++t) {
+                const int s = t % L.xs;
+                if (t >= L.xs && !mbar_wait(&x_empty[s], (t / L.xs - 1) & 1, abort_flag)) {
+                    break;
+                }
+                const int mt = blockIdx.x + t * gridDim.x;
+                mbar_arrive_expect_tx(&x_full[s], L.xpan * 16384);
+                for (int pn = 0; pn < L.xpan; ++pn) {
+                    tma_load_3d(smem + L.x + (s * L.xpan + pn) * 16384, &tm_x, &x_full[s],
+                                pn * 64, mt * 128, 0);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == kDxrMma) {
+        // whole warp, converged: MMAs and commits are elect.sync-issued
+        const uint32_t kIdRec = idesc_f16(128, 128, false, true, E::kBf16);
+        const uint32_t kIdDx = idesc_f16(128, K, false, false, E::kBf16);
+        const uint64_t ones = attn::interleave16_kmajor(sbase + L.ones);
+        const int ksteps = K / 16;
+        const uint32_t pair_lbo = static_cast<uint32_t>(nch * K * 128); // wp_j -> wg_j
+        // dx MMAs of chunk h (tile h / nch, chunk h % nch)
+        auto issue_dx = [&](int h) -> bool {
+            const int th = h / nch, jh = h - th * nch;
+            if (!mbar_wait_w(&ds_full[h & 1], (h >> 1) & 1, abort_flag)) {
+                return false;
+            }
+            if (jh == 0 && th >= 2 &&
+                !mbar_wait_w(&dx_empty[th & 1], ((th >> 1) + 1) & 1, abort_flag)) {
+                return false;
+            }
+            tc_fence_after();
+            const uint32_t pg = tmem + (h & 1) * 128;
+            const uint32_t d = tmem + 256 + (th & 1) * 128;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                // dp of columns [16 ks, 16 ks + 16) sits in the columns of epilogue warp
+                // 16 ks / kDxrCols, packed: dp in its first half, dg in its second
+                const uint32_t a = pg + kDxrCols * ((16 * ks) / kDxrCols) + ((16 * ks) % kDxrCols) / 2;
+                const uint32_t boff = jh * K * 128 + ks * 32;
+                umma_ts_w(d, a, smem_desc(sbase + L.w + boff, 16, 1024, kSwizzle128), kIdDx,
+                          (jh > 0 || ks > 0) ? 1u : 0u);
+                umma_ts_w(d, a + kDxrCols / 2,
+                          smem_desc(sbase + L.w + nch * K * 128 + boff, 16, 1024, kSwizzle128),
+                          kIdDx, 1u);
+            }
+            if (jh == nch - 1) {
+                umma_commit_w(&dx_full[th & 1]);
+            }
+            return true;
+        };
+        if (!mbar_wait_w(w_full, 0, abort_flag)) {
+            goto done;
+        }
+        int g = 0;
+        for (int t = 0; t < n_mine; ++t) {
+            const int s = t % L.xs;
+            if (!mbar_wait_w(&x_full[s], (t / L.xs) & 1, abort_flag)) {
+                goto done;
+            }
+            tc_fence_after();
+            const uint32_t xb = sbase + L.x + s * L.xpan * 16384;
+            for (int j = 0; j < nch; ++j, ++g) {
+                const uint32_t pg = tmem + (g & 1) * 128;
+                const uint32_t wj = sbase + L.w + j * K * 128;
+                for (int ks = 0; ks < ksteps; ++ks) {
+                    umma_ss_w(pg, x_desc(xb, ks),
+                              smem_desc(wj + ks * 2048, pair_lbo, 1024, kSwizzle128), kIdRec,
+                              ks > 0 ? 1u : 0u);
+                }
+                umma_ss_w(pg, ones, brow_desc(sbase + L.brow + j * 4096, 0), kIdRec, 1u);
+                umma_commit_w(&pg_full[g & 1]);
+                if (j == nch - 1) {
+                    umma_commit_w(&x_empty[s]);
+                }
+                if (g >= 1 && !issue_dx(g - 1)) {
+                    goto done;
+                }
+            }
+        }
+        if (g >= 1 && !issue_dx(g - 1)) {
+            goto done;
+        }
+    } else {
+        const int sl = warp >> 2; // column slice of the chunk: [32 sl, 32 sl + 32)
+        const int r = static_cast<int>(attn::warp_lane_base()) + lane;
+        const uint32_t lane_off = attn::warp_lane_base() << 16;
+        const int total = n_mine * nch;
+        // dout of chunk h for this thread: row of tile h / nch, 32 columns
+        auto load_dout = [&](int h, uint4 (&v)[4]) {
+            const int th = h / nch, jh = h - th * nch;
+            const int row = (static_cast<int>(blockIdx.x) + th * static_cast<int>(gridDim.x)) * 128 + r;
+            const int c0 = 64 * jh + kDxrCols * sl;
+            const uint16_t* src = dout + static_cast<int64_t>(row) * N + c0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                v[q] = (row < M && c0 + 8 * q < N) ? ld_global_stream_v4(src + 8 * q)
+                                                   : make_uint4(0u, 0u, 0u, 0u);
+            }
+        };
+        // dx of tile t: this warp stores columns [K/2 sl, K/2 sl + K/2) of row r
+        auto drain = [&](int t) -> bool {
+            if (!mbar_wait(&dx_full[t & 1], (t >> 1) & 1, abort_flag)) {
+                return false;
+            }
+            __syncwarp();
+            tc_fence_after();
+            const int row = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * 128 + r;
+            const int half = K / 2;
+            const uint32_t src = tmem + lane_off + 256 + (t & 1) * 128 + sl * half;
+            for (int q = 0; q < half; q += 8) {
+                uint32_t v[8];
+                tmem_ld8(src + q, v);
+                tmem_ld_wait();
+                if (row < M) {
+                    st_global_v4(dx + static_cast<int64_t>(row) * K + sl * half + q,
+                                 make_uint4(E::pack(__uint_as_float(v[0]), __uint_as_float(v[1])),
+                                            E::pack(__uint_as_float(v[2]), __uint_as_float(v[3])),
+                                            E::pack(__uint_as_float(v[4]), __uint_as_float(v[5])),
+                                            E::pack(__uint_as_float(v[6]), __uint_as_float(v[7]))));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&dx_empty[t & 1]);
+            }
+            return true;
+        };
+        uint4 dn[4];
+        if (total > 0) {
+            load_dout(0, dn);
+        }
+        float mk = 0.f;
+        for (int h = 0; h < total; ++h) {
+            const int th = h / nch, jh = h - th * nch;
+            if (jh == 0) {
+                const int row = (static_cast<int>(blockIdx.x) + th * static_cast<int>(gridDim.x)) * 128 + r;
+                mk = row < M ? E::to_float(mask[row]) : 0.f;
+                // the next tile's dout lines of this row, into L2
+                const int nrow = row + static_cast<int>(gridDim.x) * 128;
+                if (th + 1 < n_mine && nrow < M) {
+                    for (int c = 64 * sl; c < N; c += 128) {
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(dout + static_cast<int64_t>(nrow) * N + c));
+                    }
+                }
+            }
+            uint4 dc[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                dc[q] = dn[q];
+            }
+            if (h + 1 < total) {
+                load_dout(h + 1, dn);
+            }
+            if (!mbar_wait(&pg_full[h & 1], (h >> 1) & 1, abort_flag)) {
+                goto done;
+            }
+            __syncwarp();
+            tc_fence_after();
+            const uint32_t pg = tmem + lane_off + (h & 1) * 128 + kDxrCols * sl;
+            uint32_t pv[32], gv[32];
+            tmem_ld32(pg, pv);
+            tmem_ld32(pg + 64, gv);
+            tmem_ld_wait();
+            uint32_t op[16], og[16];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t dw[4] = {dc[q].x, dc[q].y, dc[q].z, dc[q].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 d2 = E::to_float2(dw[e]);
+                    const int c = 8 * q + 2 * e;
+                    float dp0, dg0, dp1, dg1;
+                    gate_grads(__uint_as_float(pv[c]), __uint_as_float(gv[c]), d2.x, mk, dp0, dg0);
+                    gate_grads(__uint_as_float(pv[c + 1]), __uint_as_float(gv[c + 1]), d2.y, mk, dp1, dg1);
+                    op[4 * q + e] = E::pack(dp0, dp1);
+                    og[4 * q + e] = E::pack(dg0, dg1);
+                }
+            }
+            tmem_st16(pg, op);
+            tmem_st16(pg + kDxrCols / 2, og);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&ds_full[h & 1]);
+            }
+            if (jh == 0 && th >= 1 && !drain(th - 1)) {
+                goto done;
+            }
+        }
+        if (n_mine > 0 && !drain(n_mine - 1)) {
+            goto done;
+        }
+    }
+done:
+    __syncwarp();
+    if (*abort_flag) {
+        const unsigned long long t0 = global_ns();
+        while (global_ns() - t0 < 200000ull) {
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kDxrMma) {
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // dwp, dwg, dbp, dbg for one 64-column chunk per CTA (a group of CTAs per chunk, each over a
 // strided set of row tiles); per-CTA sums are added into the zeroed f32 outputs at the end.
 // ------------------------------------------------------------------------------------------
@@ -1173,7 +1501,16 @@ int gdp_bwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const vo
                          "gdp dout"));
     tdo64 = tdo;
     const int n_mt = (M + 127) / 128;
-    {
+    if (dxr_layout(K, N).total <= 227 * 1024) {
+        const DxrLayout L = dxr_layout(K, N);
+        auto kern = gdp_bwd_dxr_kernel<T>;
+        CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
+                                 "gdp_bwd_dxr"));
+        const int grid = std::min(n_mt, dev.num_sms);
+        kern<<<grid, kDxrThreads, L.total, st>>>(tx, twp, twg, bps, bgs, ms, dos,
+                                                 static_cast<uint16_t*>(dx), M, K, N);
+        CFK_TRY(check_launch("gdp_bwd_dxr"));
+    } else {
         const DxLayout L = dx_layout(K);
         auto kern = gdp_bwd_dx_kernel<T>;
         CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,

@@ -463,6 +463,13 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// 1 / x by the rcp.approx.ftz instruction (at most 1 ulp from the rounded quotient).
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t elect_lane0() {
     return (threadIdx.x & 31u) == 0u;
 }
