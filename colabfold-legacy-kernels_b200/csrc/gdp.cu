@@ -1033,10 +1033,10 @@ __host__ __device__ inline DwLayout dw_layout(int K) {
     DwLayout L;
     L.x = 0;                  // 2 stages x 2 panels x 16 KB
     L.dout = 65536;           // 2 stages x [128 x 64] (one 16 KB panel)
-    L.hi_p = L.dout + 32768;  // four [128 x 64] bf16 tiles
-    L.lo_p = L.hi_p + 16384;
-    L.hi_g = L.lo_p + 16384;
-    L.lo_g = L.hi_g + 16384;
+    L.hi_p = L.dout + 32768;  // four [128 x 64] bf16 tiles; hi_p | hi_g and lo_p | lo_g are
+    L.hi_g = L.hi_p + 16384;  // the two 64-column atoms of one N = 128 MMA operand
+    L.lo_p = L.hi_g + 16384;
+    L.lo_g = L.lo_p + 16384;
     L.wp = L.lo_g + 16384;    // [K rows x 64 n] = K x 128 B
     L.wg = L.wp + K * 128;
     L.bp = L.wg + K * 128;    // [16 x 64] interleave, 2 KB
@@ -1165,8 +1165,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kMmaWarp) {
         // whole warp, converged: MMAs and commits are elect.sync-issued
         {
-            constexpr uint32_t kIdRec = idesc_f16(128, 64, false, true, E::kBf16);
-            constexpr uint32_t kIdDw = idesc_f16(128, 64, true, true, E::kBf16);
+            // [p | g] and [dwp | dwg] as one N = 128 MMA each: wp | wg, bp | bg, hi_p | hi_g and
+            // lo_p | lo_g are 64-column atoms at a fixed distance in shared memory
+            constexpr uint32_t kIdRec = idesc_f16(128, 128, false, true, E::kBf16);
+            constexpr uint32_t kIdDw = idesc_f16(128, 128, true, true, E::kBf16);
             const uint64_t ones = attn::interleave16_kmajor(sbase + L.ones);
             const int ksteps = K / 16;
             if (!mbar_wait_w(w_full, 0, abort_flag)) {
@@ -1179,10 +1181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int ks = 0; ks < 8; ++ks) {
                     const uint64_t a = smem_desc(xs + ks * 2048, 16384, 1024, kSwizzle128);
                     const uint32_t acc = (i > 0 || ks > 0) ? 1u : 0u;
-                    umma_ss_w(tmem + 256, a, smem_desc(sbase + L.hi_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
-                    umma_ss_w(tmem + 256, a, smem_desc(sbase + L.lo_p + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
-                    umma_ss_w(tmem + 320, a, smem_desc(sbase + L.hi_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, acc);
-                    umma_ss_w(tmem + 320, a, smem_desc(sbase + L.lo_g + ks * 2048, 16, 1024, kSwizzle128), kIdDw, 1);
+                    umma_ss_w(tmem + 256, a, smem_desc(sbase + L.hi_p + ks * 2048, 16384, 1024, kSwizzle128), kIdDw, acc);
+                    umma_ss_w(tmem + 256, a, smem_desc(sbase + L.lo_p + ks * 2048, 16384, 1024, kSwizzle128), kIdDw, 1);
                 }
                 umma_commit_w(dw_done);
                 umma_commit_w(&in_empty[i & 1]);
@@ -1200,10 +1200,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_ss_w(pg, x_desc(xs, ks), smem_desc(sbase + L.wp + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
                 }
                 umma_ss_w(pg, ones, smem_desc(sbase + L.bp, 128, 256, kInterleave), kIdRec, 1);
-                for (int ks = 0; ks < ksteps; ++ks) {
-                    umma_ss_w(pg + 64, x_desc(xs, ks), smem_desc(sbase + L.wg + ks * 2048, K * 128, 1024, kSwizzle128), kIdRec, ks > 0);
-                }
-                umma_ss_w(pg + 64, ones, smem_desc(sbase + L.bg, 128, 256, kInterleave), kIdRec, 1);
                 umma_commit_w(&rec_full[s]);
                 if (i > 0) {
                     // dW of tile i-1 once its epilogue has written the hi / lo tiles
@@ -1236,10 +1232,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 !mbar_wait(&in_full[i & 1], (i >> 1) & 1, abort_flag)) {
                 goto done;
             }
-            // hi / lo tiles are free once the dw MMAs of tile i-1 are done
-            if (i > 0 && !mbar_wait(dw_done, (i - 1) & 1, abort_flag)) {
-                goto done;
-            }
             __syncwarp();
             tc_fence_after();
             float vp[32], vg[32];
@@ -1264,6 +1256,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    mk, vp[j + 1], vg[j + 1]);
                     }
                 }
+            }
+            // hi / lo tiles are free once the dw MMAs of tile i-1 are done (the gate gradients
+            // above overlap them)
+            if (i > 0 && !mbar_wait(dw_done, (i - 1) & 1, abort_flag)) {
+                goto done;
             }
             // hi + lo split (16-bit each) into the four MMA operand tiles
             const uint32_t rowoff = r * 128;
