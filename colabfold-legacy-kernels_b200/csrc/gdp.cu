@@ -401,6 +401,17 @@ __device__ __forceinline__ void gate_grads(float p, float g, float dout, float m
     dg = dm * p * s * (1.f - s);
 }
 
+// gate_grads for two adjacent columns of a row, in f32x2 arithmetic (dg = dp * p * (1 - s)).
+__device__ __forceinline__ void gate_grads2(float2 p, float2 g, float2 dout, float m, float2& dp,
+                                            float2& dg) {
+    const float2 t = fmul2(g, make_float2(-kLog2e, -kLog2e));
+    const float2 e = fadd2(make_float2(ex2(t.x), ex2(t.y)), make_float2(1.f, 1.f));
+    const float2 sg = make_float2(rcp_approx(e.x), rcp_approx(e.y));
+    dp = fmul2(fmul2(dout, make_float2(m, m)), sg);
+    const float2 oms = ffma2(sg, make_float2(-1.f, -1.f), make_float2(1.f, 1.f));
+    dg = fmul2(fmul2(dp, p), oms);
+}
+
 // bias-row operand of one 128- or 64-column chunk, built in shared memory by one warp:
 // MN-major interleave [16 x cols], row 0 = bias[n0 + n] (0 beyond N), rows 1..15 = 0.
 __device__ __forceinline__ void build_brow(uint16_t* dst, const uint16_t* bias, int n0, int cols,
@@ -981,13 +992,13 @@ __global__ void __launch_bounds__(kDxrThreads, 1)
                 const uint32_t dw[4] = {dc[q].x, dc[q].y, dc[q].z, dc[q].w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float2 d2 = E::to_float2(dw[e]);
                     const int c = 8 * q + 2 * e;
-                    float dp0, dg0, dp1, dg1;
-                    gate_grads(__uint_as_float(pv[c]), __uint_as_float(gv[c]), d2.x, mk, dp0, dg0);
-                    gate_grads(__uint_as_float(pv[c + 1]), __uint_as_float(gv[c + 1]), d2.y, mk, dp1, dg1);
-                    op[4 * q + e] = E::pack(dp0, dp1);
-                    og[4 * q + e] = E::pack(dg0, dg1);
+                    float2 dp2, dg2;
+                    gate_grads2(make_float2(__uint_as_float(pv[c]), __uint_as_float(pv[c + 1])),
+                                make_float2(__uint_as_float(gv[c]), __uint_as_float(gv[c + 1])),
+                                E::to_float2(dw[e]), mk, dp2, dg2);
+                    op[4 * q + e] = E::pack(dp2.x, dp2.y);
+                    og[4 * q + e] = E::pack(dg2.x, dg2.y);
                 }
             }
             tmem_st16(pg, op);
@@ -1222,7 +1233,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int w = warp >> 2;
         const int r = static_cast<int>(attn::warp_lane_base()) + lane;
         const uint32_t lane_off = attn::warp_lane_base() << 16;
-        float colsum_p = 0.f, colsum_g = 0.f; // this lane's column of the warp's 32 columns
+        // bias gradients: this thread's row summed over its tiles, per column (pairs)
+        float2 accp[16], accg[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            accp[j] = make_float2(0.f, 0.f);
+            accg[j] = make_float2(0.f, 0.f);
+        }
         for (int i = 0; i < n_mine; ++i) {
             const int mt = group + i * n_groups;
             const int row = mt * 128 + r;
@@ -1234,7 +1251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __syncwarp();
             tc_fence_after();
-            float vp[32], vg[32];
+            float2 vp[16], vg[16]; // dp, dg of columns (2j, 2j + 1)
             {
                 uint32_t pv[32], gv[32];
                 const uint32_t pg = tmem + lane_off + (i & 1) * 128 + 32 * w;
@@ -1248,14 +1265,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t dww[4] = {dw4.x, dw4.y, dw4.z, dw4.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float2 d2 = E::to_float2(dww[e]);
-                        const int j = 8 * h + 2 * e;
-                        gate_grads(__uint_as_float(pv[j]), __uint_as_float(gv[j]), d2.x, mk,
-                                   vp[j], vg[j]);
-                        gate_grads(__uint_as_float(pv[j + 1]), __uint_as_float(gv[j + 1]), d2.y,
-                                   mk, vp[j + 1], vg[j + 1]);
+                        const int j = 4 * h + e;
+                        gate_grads2(make_float2(__uint_as_float(pv[2 * j]), __uint_as_float(pv[2 * j + 1])),
+                                    make_float2(__uint_as_float(gv[2 * j]), __uint_as_float(gv[2 * j + 1])),
+                                    E::to_float2(dww[e]), mk, vp[j], vg[j]);
                     }
                 }
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                accp[j] = fadd2(accp[j], vp[j]);
+                accg[j] = fadd2(accg[j], vg[j]);
             }
             // hi / lo tiles are free once the dw MMAs of tile i-1 are done (the gate gradients
             // above overlap them)
@@ -1269,13 +1289,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t hp[4], lp[4], hg[4], lg[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int j = 8 * h + 2 * e;
-                    hp[e] = E::pack(vp[j], vp[j + 1]);
-                    hg[e] = E::pack(vg[j], vg[j + 1]);
-                    const float2 bpf = E::to_float2(hp[e]);
-                    const float2 bgf = E::to_float2(hg[e]);
-                    lp[e] = E::pack(vp[j] - bpf.x, vp[j + 1] - bpf.y);
-                    lg[e] = E::pack(vg[j] - bgf.x, vg[j + 1] - bgf.y);
+                    const int j = 4 * h + e;
+                    hp[e] = E::pack(vp[j].x, vp[j].y);
+                    hg[e] = E::pack(vg[j].x, vg[j].y);
+                    const float2 rp = ffma2(E::to_float2(hp[e]), make_float2(-1.f, -1.f), vp[j]);
+                    const float2 rg = ffma2(E::to_float2(hg[e]), make_float2(-1.f, -1.f), vg[j]);
+                    lp[e] = E::pack(rp.x, rp.y);
+                    lg[e] = E::pack(rg.x, rg.y);
                 }
                 const uint32_t off = rowoff + (((4 * w + h) ^ (r & 7)) << 4);
                 attn::sts128(sbase + L.hi_p + off, make_uint4(hp[0], hp[1], hp[2], hp[3]));
@@ -1289,13 +1309,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) {
                 mbar_arrive(ds_full);
             }
-            // bias gradients: column sums over this warp's 32 rows
-            colsum_p += warp_column_sum32(vp, lane);
-            colsum_g += warp_column_sum32(vg, lane);
         }
-        // combine the 4 row quarters of each warpgroup, then add into the outputs
-        red[warp * 64 + lane] = colsum_p;
-        red[warp * 64 + 32 + lane] = colsum_g;
+        {
+            // column sums over this warp's 32 rows, then over the 4 row quarters of each warpgroup
+            float cp[32], cg[32];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                cp[2 * j] = accp[j].x;
+                cp[2 * j + 1] = accp[j].y;
+                cg[2 * j] = accg[j].x;
+                cg[2 * j + 1] = accg[j].y;
+            }
+            red[warp * 64 + lane] = warp_column_sum32(cp, lane);
+            red[warp * 64 + 32 + lane] = warp_column_sum32(cg, lane);
+        }
         named_bar_sync(1, 256);
         if (threadIdx.x < 64) {
             const int ww = threadIdx.x / 32, col = threadIdx.x % 32;
