@@ -909,16 +909,38 @@ __global__ void __launch_bounds__(kDxrThreads, 1)
         const int r = static_cast<int>(attn::warp_lane_base()) + lane;
         const uint32_t lane_off = attn::warp_lane_base() << 16;
         const int total = n_mine * nch;
+        const bool wide = (N % 16 == 0) && (reinterpret_cast<uintptr_t>(dout) & 31) == 0;
+        const bool dx32 = (reinterpret_cast<uintptr_t>(dx) & 31) == 0;
         // dout of chunk h for this thread: row of tile h / nch, 32 columns
-        auto load_dout = [&](int h, uint4 (&v)[4]) {
+        // (32-byte loads when the rows allow them: fewer, fully used sectors per instruction)
+        auto load_dout = [&](int h, uint32_t (&v)[16]) {
             const int th = h / nch, jh = h - th * nch;
             const int row = (static_cast<int>(blockIdx.x) + th * static_cast<int>(gridDim.x)) * 128 + r;
             const int c0 = 64 * jh + kDxrCols * sl;
             const uint16_t* src = dout + static_cast<int64_t>(row) * N + c0;
+            if (wide) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                v[q] = (row < M && c0 + 8 * q < N) ? ld_global_stream_v4(src + 8 * q)
-                                                   : make_uint4(0u, 0u, 0u, 0u);
+                for (int q = 0; q < 2; ++q) {
+                    uint32_t (&w8)[8] = *reinterpret_cast<uint32_t (*)[8]>(&v[8 * q]);
+                    if (row < M && c0 + 16 * q < N) {
+                        ld_global_nc_v8(src + 16 * q, w8);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            w8[e] = 0u;
+                        }
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 u = (row < M && c0 + 8 * q < N) ? ld_global_nc_v4(src + 8 * q)
+                                                                : make_uint4(0u, 0u, 0u, 0u);
+                    v[4 * q] = u.x;
+                    v[4 * q + 1] = u.y;
+                    v[4 * q + 2] = u.z;
+                    v[4 * q + 3] = u.w;
+                }
             }
         };
         // dx of tile t: this warp stores columns [K/2 sl, K/2 sl + K/2) of row r
@@ -931,16 +953,38 @@ __global__ void __launch_bounds__(kDxrThreads, 1)
             const int row = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * 128 + r;
             const int half = K / 2;
             const uint32_t src = tmem + lane_off + 256 + (t & 1) * 128 + sl * half;
-            for (int q = 0; q < half; q += 8) {
-                uint32_t v[8];
-                tmem_ld8(src + q, v);
-                tmem_ld_wait();
-                if (row < M) {
-                    st_global_v4(dx + static_cast<int64_t>(row) * K + sl * half + q,
-                                 make_uint4(E::pack(__uint_as_float(v[0]), __uint_as_float(v[1])),
-                                            E::pack(__uint_as_float(v[2]), __uint_as_float(v[3])),
-                                            E::pack(__uint_as_float(v[4]), __uint_as_float(v[5])),
-                                            E::pack(__uint_as_float(v[6]), __uint_as_float(v[7]))));
+            uint16_t* dst = dx + static_cast<int64_t>(row) * K + sl * half;
+            if (half % 32 == 0 && dx32) {
+                // 32 columns per tensor-memory load, 32-byte stores
+                for (int q = 0; q < half; q += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(src + q, v);
+                    tmem_ld_wait();
+                    if (row < M) {
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            uint32_t o[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                o[e] = E::pack(__uint_as_float(v[16 * u + 2 * e]),
+                                               __uint_as_float(v[16 * u + 2 * e + 1]));
+                            }
+                            st_global_v8(dst + q + 16 * u, o);
+                        }
+                    }
+                }
+            } else {
+                for (int q = 0; q < half; q += 8) {
+                    uint32_t v[8];
+                    tmem_ld8(src + q, v);
+                    tmem_ld_wait();
+                    if (row < M) {
+                        st_global_v4(dst + q,
+                                     make_uint4(E::pack(__uint_as_float(v[0]), __uint_as_float(v[1])),
+                                                E::pack(__uint_as_float(v[2]), __uint_as_float(v[3])),
+                                                E::pack(__uint_as_float(v[4]), __uint_as_float(v[5])),
+                                                E::pack(__uint_as_float(v[6]), __uint_as_float(v[7]))));
+                    }
                 }
             }
             tc_fence_before();
@@ -950,9 +994,13 @@ __global__ void __launch_bounds__(kDxrThreads, 1)
             }
             return true;
         };
-        uint4 dn[4];
+        // dout of the next two chunks in flight
+        uint32_t dn[16], dn2[16];
         if (total > 0) {
             load_dout(0, dn);
+        }
+        if (total > 1) {
+            load_dout(1, dn2);
         }
         float mk = 0.f;
         for (int h = 0; h < total; ++h) {
@@ -968,13 +1016,14 @@ __global__ void __launch_bounds__(kDxrThreads, 1)
                     }
                 }
             }
-            uint4 dc[4];
+            uint32_t dc[16];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < 16; ++q) {
                 dc[q] = dn[q];
+                dn[q] = dn2[q];
             }
-            if (h + 1 < total) {
-                load_dout(h + 1, dn);
+            if (h + 2 < total) {
+                load_dout(h + 2, dn2);
             }
             if (!mbar_wait(&pg_full[h & 1], (h >> 1) & 1, abort_flag)) {
                 goto done;
@@ -989,7 +1038,7 @@ __global__ void __launch_bounds__(kDxrThreads, 1)
             uint32_t op[16], og[16];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const uint32_t dw[4] = {dc[q].x, dc[q].y, dc[q].z, dc[q].w};
+                const uint32_t* dw = dc + 4 * q;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int c = 8 * q + 2 * e;
