@@ -12,11 +12,15 @@
 // times a bias row, so the epilogue only evaluates mask * p * sigmoid(g) and stores.
 //
 // Backward (tcgen05, two kernels, both recompute p and g from x):
-//   gdp_bwd_dx: dp = dout*mask*s, dg = dout*mask*p*s*(1-s) into shared memory, then
-//               dx += dp wp^T + dg wg^T over the column chunks in tensor memory.
+//   gdp_bwd_dxr: both weight matrices resident in shared memory; per 64-column chunk one
+//               N = 128 MMA chain gives [p | g], the epilogue writes dp = dout*mask*s and
+//               dg = dout*mask*p*s*(1-s) back into tensor memory as 16-bit pairs, and
+//               dx += dp wp^T + dg wg^T runs with A in tensor memory.  Shapes whose weights do
+//               not fit take gdp_bwd_dx, which streams 128-column weight chunks and stages
+//               dp, dg in shared memory.
 //   gdp_bwd_dw: per 64-column chunk (a group of CTAs per chunk), dp and dg split into
-//               bf16 hi + lo parts so that dwp = x^T dp, dwg = x^T dg and the bias gradients
-//               (ones^T dp, ones^T dg) keep f32 accuracy; per-CTA sums are added at the end.
+//               bf16 hi + lo parts so that dwp = x^T dp, dwg = x^T dg keep f32 accuracy; the
+//               bias gradients are f32 column sums; per-CTA sums are added at the end.
 //
 // Shapes outside the fast paths (K not a multiple of 16 or above 128, weights larger than the
 // shared-memory budget, unaligned pointers) take plain CUDA-core kernels.
