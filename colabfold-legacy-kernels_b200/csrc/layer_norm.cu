@@ -386,21 +386,43 @@ __global__ __launch_bounds__(kThreads) void ln_bwd_generic_kernel(
 }
 
 // Sums the per-CTA partials in a fixed order: dgamma = sum_b partial[b][c],
-// dbeta = sum_b partial[b][C + c].
-__global__ void ln_bwd_reduce_kernel(const float* __restrict__ partial, int nparts, int C,
-                                     float* __restrict__ dgamma, float* __restrict__ dbeta) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= 2 * C) {
-        return;
+// dbeta = sum_b partial[b][C + c].  A CTA of 32 warps owns 32 columns: warp w adds the partials
+// b = w, w + 32, ... (lane = column, coalesced rows, four chains in flight), then warp 0 adds the
+// 32 warp sums in warp order, so the result does not depend on timing.
+constexpr int kReduceWarps = 32;
+
+__global__ void __launch_bounds__(kReduceWarps * 32)
+    ln_bwd_reduce_kernel(const float* __restrict__ partial, int nparts, int C,
+                         float* __restrict__ dgamma, float* __restrict__ dbeta) {
+    __shared__ float red[kReduceWarps][33];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x * 32 + lane;
+    const int64_t stride = 2 * static_cast<int64_t>(C);
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    if (c < 2 * C) {
+        int b = warp;
+        for (; b + 3 * kReduceWarps < nparts; b += 4 * kReduceWarps) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                s[u] += partial[(b + u * kReduceWarps) * stride + c];
+            }
+        }
+        for (int u = 0; b < nparts; b += kReduceWarps, ++u) {
+            s[u & 3] += partial[b * stride + c];
+        }
     }
-    float s = 0.f;
-    for (int b = 0; b < nparts; ++b) {
-        s += partial[static_cast<int64_t>(b) * 2 * C + c];
-    }
-    if (c < C) {
-        dgamma[c] = s;
-    } else {
-        dbeta[c - C] = s;
+    red[warp][lane] = (s[0] + s[1]) + (s[2] + s[3]);
+    __syncthreads();
+    if (warp == 0 && c < 2 * C) {
+        float t = 0.f;
+        for (int w = 0; w < kReduceWarps; ++w) {
+            t += red[w][lane];
+        }
+        if (c < C) {
+            dgamma[c] = t;
+        } else {
+            dbeta[c - C] = t;
+        }
     }
 }
 
@@ -539,10 +561,9 @@ int ln_bwd_impl(cudaStream_t st, const DeviceInfo& d, const void* x, const float
                                                                partial, M, static_cast<int>(C), eps);
     }
     CFK_TRY(check_launch("ln_bwd"));
-    const int threads = 256;
-    const int blocks = static_cast<int>((2 * C + threads - 1) / threads);
-    ln_bwd_reduce_kernel<<<blocks, threads, 0, st>>>(partial, grid, static_cast<int>(C), dgamma,
-                                                     dbeta);
+    const int blocks = static_cast<int>((2 * C + 31) / 32);
+    ln_bwd_reduce_kernel<<<blocks, kReduceWarps * 32, 0, st>>>(partial, grid, static_cast<int>(C),
+                                                               dgamma, dbeta);
     return check_launch("ln_bwd_reduce");
 }
 
@@ -727,10 +748,9 @@ int ln_bwd_noalloc_impl(cudaStream_t st, const DeviceInfo& d, const void* x, con
                                                                partial, M, static_cast<int>(C), eps);
     }
     CFK_TRY(check_launch("ln_bwd_noalloc"));
-    const int threads = 256;
-    const int blocks = static_cast<int>((2 * C + threads - 1) / threads);
-    ln_bwd_reduce_kernel<<<blocks, threads, 0, st>>>(partial, grid, static_cast<int>(C), dgamma,
-                                                     dbeta);
+    const int blocks = static_cast<int>((2 * C + 31) / 32);
+    ln_bwd_reduce_kernel<<<blocks, kReduceWarps * 32, 0, st>>>(partial, grid, static_cast<int>(C),
+                                                               dgamma, dbeta);
     return check_launch("ln_bwd_noalloc_reduce");
 }
 
