@@ -1112,6 +1112,29 @@ __host__ __device__ inline DwLayout dw_layout(int K) {
     return L;
 }
 
+// Warp roles of the dW kernel: 4*EQ epilogue warps (EQ per tensor-memory lane quarter, each
+// with 64/EQ columns of the chunk), then the producer and the MMA warp.
+template <int EQ>
+struct DwWarps {
+    static constexpr int kEpi = 4 * EQ;
+    static constexpr int kProducer = kEpi;
+    static constexpr int kMma = kEpi + 1;
+    static constexpr int kThreads = (kEpi + 2) * 32;
+    static constexpr int kCols = 64 / EQ;
+};
+constexpr int kDwEq = 4;
+constexpr int kDwPrefetch = 4; // row tiles prefetched into L2 ahead of the loads
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 32) {
+        tmem_ld32(taddr, r);
+    } else {
+        static_assert(N == 16, "16 or 32 columns");
+        tmem_ld16(taddr, r);
+    }
+}
+
 // Column sums of v[0..31] over the 32 lanes: afterwards lane l holds the sum of column l.
 __device__ __forceinline__ float warp_column_sum32(float (&v)[32], int lane) {
 #pragma unroll
@@ -1127,8 +1150,30 @@ __device__ __forceinline__ float warp_column_sum32(float (&v)[32], int lane) {
     return v[0];
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 1)
+// Column sums of v[0..N) over the 32 lanes: afterwards lane l (l < N) holds the sum of column l.
+template <int N>
+__device__ __forceinline__ float warp_column_sum(float (&v)[N], int lane) {
+    if constexpr (N == 32) {
+        return warp_column_sum32(v, lane);
+    } else {
+        static_assert(N == 16, "16 or 32 columns");
+#pragma unroll
+        for (int s = 8; s >= 1; s >>= 1) {
+            const bool up = (lane & s) != 0;
+#pragma unroll
+            for (int i = 0; i < s; ++i) {
+                const float send = up ? v[i] : v[i + s];
+                const float keep = up ? v[i + s] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+            }
+        }
+        // lanes l and l ^ 16 hold the two half-warp sums of column l & 15
+        return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 16);
+    }
+}
+
+template <typename T, int EQ>
+__global__ void __launch_bounds__(DwWarps<EQ>::kThreads, 1)
     gdp_bwd_dw_kernel(const __grid_constant__ CUtensorMap tm_x,
                       const __grid_constant__ CUtensorMap tm_wp,
                       const __grid_constant__ CUtensorMap tm_wg,
@@ -1138,6 +1183,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                       float* __restrict__ dwg, float* __restrict__ dbp, float* __restrict__ dbg,
                       int M, int K, int N, int n_groups) {
     using E = Elem<T>;
+    using WR = DwWarps<EQ>;
+    constexpr int kMmaWarp = WR::kMma;
+    constexpr int kProducerWarp = WR::kProducer;
+    constexpr int CW = WR::kCols;   // columns of the 64-column chunk per epilogue warp
+    constexpr int NJ = CW / 2;      // column pairs
+    constexpr int NH = CW / 8;      // 16-byte chunks
     const DwLayout L = dw_layout(K);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1168,7 +1219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&in_empty[s], 1);
             mbar_init(&rec_full[s], 1);
         }
-        mbar_init(ds_full, 8);
+        mbar_init(ds_full, WR::kEpi);
         mbar_init(dw_done, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -1215,6 +1266,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < n_mine; ++i) {
                 const int mt = group + i * n_groups;
                 const int s = i & 1;
+                // the tiles kDwPrefetch ahead into L2: the two stages alone cannot cover the
+                // load latency of a streaming GPU
+                for (int ip = (i == 0 ? 1 : i + kDwPrefetch); ip <= i + kDwPrefetch && ip < n_mine; ++ip) {
+                    const int mp = group + ip * n_groups;
+                    for (int pn = 0; pn < panels; ++pn) {
+                        tma_prefetch_l2_3d(&tm_x, pn * 64, mp * 128, 0);
+                    }
+                    tma_prefetch_l2_3d(&tm_dout, n0, mp * 128, 0);
+                }
                 if (i >= 2 && !mbar_wait(&in_empty[s], ((i >> 1) - 1) & 1, abort_flag)) {
                     goto done;
                 }
@@ -1287,9 +1347,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = static_cast<int>(attn::warp_lane_base()) + lane;
         const uint32_t lane_off = attn::warp_lane_base() << 16;
         // bias gradients: this thread's row summed over its tiles, per column (pairs)
-        float2 accp[16], accg[16];
+        float2 accp[NJ], accg[NJ];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < NJ; ++j) {
             accp[j] = make_float2(0.f, 0.f);
             accg[j] = make_float2(0.f, 0.f);
         }
@@ -1304,17 +1364,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __syncwarp();
             tc_fence_after();
-            float2 vp[16], vg[16]; // dp, dg of columns (2j, 2j + 1)
+            float2 vp[NJ], vg[NJ]; // dp, dg of columns (2j, 2j + 1) of this warp's slice
             {
-                uint32_t pv[32], gv[32];
-                const uint32_t pg = tmem + lane_off + (i & 1) * 128 + 32 * w;
-                tmem_ld32(pg, pv);
-                tmem_ld32(pg + 64, gv);
+                uint32_t pv[CW], gv[CW];
+                const uint32_t pg = tmem + lane_off + (i & 1) * 128 + CW * w;
+                tmem_ld_cols(pg, pv);
+                tmem_ld_cols(pg + 64, gv);
                 tmem_ld_wait();
                 const uint32_t do_row = sbase + L.dout + (i & 1) * 16384 + r * 128;
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    const uint4 dw4 = attn::lds128(do_row + (((4 * w + h) ^ (r & 7)) << 4));
+                for (int h = 0; h < NH; ++h) {
+                    const uint4 dw4 = attn::lds128(do_row + (((NH * w + h) ^ (r & 7)) << 4));
                     const uint32_t dww[4] = {dw4.x, dw4.y, dw4.z, dw4.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
@@ -1326,7 +1386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
+            for (int j = 0; j < NJ; ++j) {
                 accp[j] = fadd2(accp[j], vp[j]);
                 accg[j] = fadd2(accg[j], vg[j]);
             }
@@ -1338,7 +1398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // hi + lo split (16-bit each) into the four MMA operand tiles
             const uint32_t rowoff = r * 128;
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
+            for (int h = 0; h < NH; ++h) {
                 uint32_t hp[4], lp[4], hg[4], lg[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -1350,7 +1410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     lp[e] = E::pack(rp.x, rp.y);
                     lg[e] = E::pack(rg.x, rg.y);
                 }
-                const uint32_t off = rowoff + (((4 * w + h) ^ (r & 7)) << 4);
+                const uint32_t off = rowoff + (((NH * w + h) ^ (r & 7)) << 4);
                 attn::sts128(sbase + L.hi_p + off, make_uint4(hp[0], hp[1], hp[2], hp[3]));
                 attn::sts128(sbase + L.lo_p + off, make_uint4(lp[0], lp[1], lp[2], lp[3]));
                 attn::sts128(sbase + L.hi_g + off, make_uint4(hg[0], hg[1], hg[2], hg[3]));
@@ -1364,47 +1424,51 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         {
-            // column sums over this warp's 32 rows, then over the 4 row quarters of each warpgroup
-            float cp[32], cg[32];
+            // column sums over this warp's 32 rows, then over the 4 row quarters of each slice
+            float cp[CW], cg[CW];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
+            for (int j = 0; j < NJ; ++j) {
                 cp[2 * j] = accp[j].x;
                 cp[2 * j + 1] = accp[j].y;
                 cg[2 * j] = accg[j].x;
                 cg[2 * j + 1] = accg[j].y;
             }
-            red[warp * 64 + lane] = warp_column_sum32(cp, lane);
-            red[warp * 64 + 32 + lane] = warp_column_sum32(cg, lane);
+            const float sp = warp_column_sum<CW>(cp, lane);
+            const float sg = warp_column_sum<CW>(cg, lane);
+            if (lane < CW) {
+                red[warp * 2 * CW + lane] = sp;
+                red[warp * 2 * CW + CW + lane] = sg;
+            }
         }
-        named_bar_sync(1, 256);
+        named_bar_sync(1, WR::kEpi * 32);
         if (threadIdx.x < 64) {
-            const int ww = threadIdx.x / 32, col = threadIdx.x % 32;
+            const int ww = threadIdx.x / CW, col = threadIdx.x % CW;
             float sp = 0.f, sg = 0.f;
             for (int q = 0; q < 4; ++q) {
-                sp += red[(4 * ww + q) * 64 + col];
-                sg += red[(4 * ww + q) * 64 + 32 + col];
+                sp += red[(4 * ww + q) * 2 * CW + col];
+                sg += red[(4 * ww + q) * 2 * CW + CW + col];
             }
-            const int n = n0 + 32 * ww + col;
+            const int n = n0 + CW * ww + col;
             if (n < N && n_mine > 0) {
                 atomicAdd(dbp + n, sp);
                 atomicAdd(dbg + n, sg);
             }
         }
-        // weight gradients: thread (w, r) owns row k = r, columns [32w, 32w + 32)
+        // weight gradients: thread (w, r) owns row k = r, columns [CW w, CW w + CW)
         if (n_mine > 0) {
             if (!mbar_wait(dw_done, (n_mine - 1) & 1, abort_flag)) {
                 goto done;
             }
             __syncwarp();
             tc_fence_after();
-            uint32_t a[32], b[32];
-            tmem_ld32(tmem + lane_off + 256 + 32 * w, a);
-            tmem_ld32(tmem + lane_off + 320 + 32 * w, b);
+            uint32_t a[CW], b[CW];
+            tmem_ld_cols(tmem + lane_off + 256 + CW * w, a);
+            tmem_ld_cols(tmem + lane_off + 320 + CW * w, b);
             tmem_ld_wait();
             if (r < K) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int n = n0 + 32 * w + j;
+                for (int j = 0; j < CW; ++j) {
+                    const int n = n0 + CW * w + j;
                     if (n < N) {
                         atomicAdd(dwp + static_cast<int64_t>(r) * N + n, __uint_as_float(a[j]));
                         atomicAdd(dwg + static_cast<int64_t>(r) * N + n, __uint_as_float(b[j]));
@@ -1599,12 +1663,12 @@ int gdp_bwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const vo
     }
     {
         const DwLayout L = dw_layout(K);
-        auto kern = gdp_bwd_dw_kernel<T>;
+        auto kern = gdp_bwd_dw_kernel<T, kDwEq>;
         CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
                                  "gdp_bwd_dw"));
         const int nch = (N + 63) / 64;
         const int groups = std::max(1, std::min(n_mt, dev.num_sms / nch));
-        kern<<<nch * groups, kThreads, L.total, st>>>(tx, twp, twg, tdo64, bps, bgs, ms, dwp,
+        kern<<<nch * groups, DwWarps<kDwEq>::kThreads, L.total, st>>>(tx, twp, twg, tdo64, bps, bgs, ms, dwp,
                                                       dwg, dbp, dbg, M, K, N, groups);
         CFK_TRY(check_launch("gdp_bwd_dw"));
     }
