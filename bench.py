@@ -279,29 +279,34 @@ def run_ours(args, rank, world, local_rank):
     ev = {name: [torch.cuda.Event(enable_timing=True) for _ in range(2)]
           for name in ("step", "fwd", "bwd_main")}
 
-    def step(record=False):
+    main_set = {"q": q, "k": k, "v": v, "dout": dout, "kmask": kmask, "bias": bias, "out": out,
+                "lse": lse, "grads": grads}
+
+    def step(record=False, b=main_set):
         stream = torch.cuda.current_stream(dev)
+        bq, bk, bv, bb, bm, bo, bl, bd, bg = (b[x] for x in ("q", "k", "v", "bias", "kmask", "out",
+                                                            "lse", "dout", "grads"))
         if record:
             ev["step"][0].record(stream)
             ev["fwd"][0].record(stream)
-        torch_ops.attention_fwd(q, k, v, bias, kmask, scale, out=out, lse=lse)
+        torch_ops.attention_fwd(bq, bk, bv, bb, bm, scale, out=bo, lse=bl)
         if record:
             ev["fwd"][1].record(stream)
-        torch_ops.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=ws,
-                                grads=grads, phase=0)
+        torch_ops.attention_bwd(bq, bk, bv, bb, bm, bo, bl, bd, scale, workspace=ws,
+                                grads=bg, phase=0)
         if record:
             ev["bwd_main"][0].record(stream)
-        torch_ops.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=ws,
-                                grads=grads, phase=1)
+        torch_ops.attention_bwd(bq, bk, bv, bb, bm, bo, bl, bd, scale, workspace=ws,
+                                grads=bg, phase=1)
         if record:
             ev["bwd_main"][1].record(stream)
         if world > 1:
             # dbias is final after the main kernel: reduce it while the converts run
             comm.wait_stream(stream)
             with torch.cuda.stream(comm):
-                dist.all_reduce(grads[3])
-        torch_ops.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=ws,
-                                grads=grads, phase=2)
+                dist.all_reduce(bg[3])
+        torch_ops.attention_bwd(bq, bk, bv, bb, bm, bo, bl, bd, scale, workspace=ws,
+                                grads=bg, phase=2)
         if world > 1:
             stream.wait_stream(comm)
         if record:
@@ -353,25 +358,52 @@ def run_ours(args, rank, world, local_rank):
                              ("dbias", grads[3]))}
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = sum(t.numel() * t.element_size() for t in host_out.values())
-    e2e_ms = []
+    # Steps are pipelined over two device buffer sets: step i's host->device copies (one
+    # stream) overlap step i-1's compute and step i-2's device->host copies (two more streams);
+    # every step still copies all its inputs in and all its results out inside the timed region.
+    sets = [main_set, {x: (tuple(torch.empty_like(g) for g in t) if x == "grads"
+                           else torch.empty_like(t)) for x, t in main_set.items()}]
+    s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_comp = torch.cuda.current_stream(dev)
+    in_ev = [torch.cuda.Event() for _ in range(2)]
+    comp_ev = [torch.cuda.Event() for _ in range(2)]
+    out_ev = [torch.cuda.Event() for _ in range(2)]
+
+    def pipelined(nsteps):
+        for i in range(nsteps):
+            b = sets[i % 2]
+            with torch.cuda.stream(s_h2d):
+                if i >= 2:
+                    s_h2d.wait_event(comp_ev[i % 2])  # step i-2 is done reading this set
+                for x in ("q", "k", "v", "dout", "kmask", "bias"):
+                    b[x].copy_(host[x], non_blocking=True)
+                in_ev[i % 2].record(s_h2d)
+            s_comp.wait_event(in_ev[i % 2])
+            if i >= 2:
+                s_comp.wait_event(out_ev[i % 2])  # step i-2's results are copied out
+            step(b=b)
+            comp_ev[i % 2].record(s_comp)
+            with torch.cuda.stream(s_d2h):
+                s_d2h.wait_event(comp_ev[i % 2])
+                for x, t in (("out", b["out"]), ("dq", b["grads"][0]), ("dk", b["grads"][1]),
+                             ("dv", b["grads"][2]), ("dbias", b["grads"][3])):
+                    host_out[x].copy_(t, non_blocking=True)
+                out_ev[i % 2].record(s_d2h)
+        s_comp.wait_stream(s_d2h)
+
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for i in range(args.e2e_steps + 1):
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0.record()
-        for x, t in (("q", q), ("k", k), ("v", v), ("dout", dout), ("kmask", kmask),
-                     ("bias", bias)):
-            t.copy_(host[x], non_blocking=True)
-        step()
-        for x, t in (("out", out), ("dq", grads[0]), ("dk", grads[1]), ("dv", grads[2]),
-                     ("dbias", grads[3])):
-            host_out[x].copy_(t, non_blocking=True)
-        e1.record()
-        torch.cuda.synchronize()
-        if i > 0:  # the first is a warm-up
-            e2e_ms.append(e0.elapsed_time(e1))
-    me2e = sum(e2e_ms) / len(e2e_ms)
+    pipelined(2)  # warm-up
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(s_comp)
+    s_h2d.wait_stream(s_comp)
+    s_d2h.wait_stream(s_comp)
+    pipelined(args.e2e_steps)
+    e1.record(s_comp)
+    torch.cuda.synchronize()
+    me2e = e0.elapsed_time(e1) / args.e2e_steps
     if world > 1:
         t = torch.tensor([me2e], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -406,7 +438,9 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "flushed between steps (256 MB write, outside the timed events)"},
         "gpu_launches": 6 * args.steps,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": me2e},
+                "d2h_bytes_per_step": d2h, "ms_per_step": me2e, "steps": args.e2e_steps,
+                "overlap": "double-buffered: host->device copies of step i+1 and device->host "
+                           "copies of step i-1 run on two streams beside step i"},
         "roofline": roofline,
         "clocks": clocks.summary(),
         "wall_s_timed": wall,
@@ -521,7 +555,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--cpu-rows", type=int, default=32,
                     help="attention rows in one CPU sample (reference arm and cpu_baseline)")
     ap.add_argument("--skip-extras", action="store_true", help="skip LayerNorm/GDP lines")
