@@ -506,6 +506,21 @@ def bench_gdp(dev, pk, steps=20):
     ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
     ms = _stream_ms(lambda: torch_ops.gdp_bwd(x, wp, bp, wg, bg, mask, dout, workspace=ws),
                     steps)
+    # LayerNorm fused into the forward (cfk_ln_gdp_fwd) against LayerNorm then GDP
+    z, gamma, beta = inp["x"], inp["gamma"], inp["beta"]
+    y = torch.empty_like(z)
+    ms_fused = _stream_ms(lambda: torch_ops.ln_gdp_fwd(z, gamma, beta, 1e-5, wp, bp, wg, bg, mask,
+                                                       out=out), steps)
+    ms_two = _stream_ms(lambda: (torch_ops.layer_norm_fwd(z, gamma, beta, 1e-5, out=y),
+                                 torch_ops.gdp_fwd(y, wp, bp, wg, bg, mask, out=out)), steps)
+    fused_bytes = 2 * (m * kk + m * n + m + 2 * kk * n + 2 * n) + 8 * kk
+    t_fused = max(fused_bytes / (pk["hbm_gbs"] * 1e9),
+                  oracle.gdp.flops_fwd(m, kk, n) / (pk["bf16"] * 1e12))
+    res["ln_fwd_fused"] = {
+        "metric": "LayerNorm + GDP fwd [1M x 128 -> 256] bf16, one kernel", "ms": ms_fused,
+        "unit": "ms", "separate_ms": ms_two,
+        "roofline": {"bound": "hbm", "algorithmic_bytes": fused_bytes, "bound_ms": t_fused * 1e3,
+                     "frac": t_fused * 1e3 / ms_fused}}
     bwd_bytes = 2 * (m * kk + m * n + m * kk + m) + 4 * (2 * kk * n + 2 * n)
     dx_t, dw_t = traffic_from_profiles("gdp_bwd_dx_c4"), traffic_from_profiles("gdp_bwd_dw_c4")
     res["bwd"] = line("bwd", ms, oracle.gdp.flops_bwd(m, kk, n), bwd_bytes,

@@ -55,7 +55,7 @@ struct FwdLayout {
     int npad;      // N rounded up to 128
     int x_stage;   // one x tile: ceil(K/64) panels of 128 rows x 128 B
     int xs;        // x stages (2 when they fit beside the weights, else 1)
-    int off_x, off_wp, off_wg, off_bp, off_bg, off_ones, off_stg, off_bar, total;
+    int off_x, off_wp, off_wg, off_bp, off_bg, off_ones, off_stg, off_ln, off_bar, total;
 };
 
 __host__ __device__ inline FwdLayout fwd_layout(int K, int N) {
@@ -71,7 +71,8 @@ __host__ __device__ inline FwdLayout fwd_layout(int K, int N) {
         L.off_bg = L.off_bp + (L.npad / 8) * 256;
         L.off_ones = L.off_bg + (L.npad / 8) * 256;
         L.off_stg = L.off_ones + 4096; // output staging: one [128 x 64] box per warpgroup
-        L.off_bar = L.off_stg + 2 * 16384;
+        L.off_ln = L.off_stg + 2 * 16384; // LayerNorm gamma, beta (f32 [K] each), fused form
+        L.off_bar = L.off_ln + 2 * kMaxK * 4;
         L.total = L.off_bar + 16 * 8 + 16 + 1024;
         if (L.total <= 227 * 1024) {
             break;
@@ -96,14 +97,28 @@ __device__ __forceinline__ uint64_t brow_desc(uint32_t b, int c) {
     return smem_desc(b + c * 16 * 256, 128, 256, kInterleave);
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 1)
+// LayerNorm prologue of the fused form: z, gamma, beta, eps; optional row statistics.
+struct LnIn {
+    const uint16_t* z;
+    const float* gamma;
+    const float* beta;
+    float* mean;
+    float* rstd;
+    float eps;
+};
+
+// kLn: x = LayerNorm(z) is never written to memory.  A fourth warpgroup (warps 10-13, thread =
+// row) reads the z rows of the next tile from global memory while the MMAs of the current one
+// run, normalises them in f32 and writes the 16-bit result straight into the x stage in the
+// swizzled layout the MMA reads; the producer then loads only the weights.
+template <typename T, bool kLn>
+__global__ void __launch_bounds__(kLn ? kThreads + 128 : kThreads, 1)
     gdp_fwd_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_wp,
                    const __grid_constant__ CUtensorMap tm_wg,
                    const __grid_constant__ CUtensorMap tm_out, const uint16_t* __restrict__ bp,
                    const uint16_t* __restrict__ bg, const uint16_t* __restrict__ mask, int M,
-                   int K, int N) {
+                   int K, int N, const LnIn ln) {
     using E = Elem<T>;
     const FwdLayout L = fwd_layout(K, N);
     extern __shared__ uint8_t smem_raw[];
@@ -116,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* w_full = bars + 4;
     uint64_t* acc_full = bars + 5;  // [2]
     uint64_t* acc_empty = bars + 7; // [2]
+    uint64_t* x_ready = bars + 9;   // [2] (kLn) x of the stage normalised by the LN warpgroup
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.off_bar + 16 * 8);
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5;
@@ -129,6 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&x_empty[i], 1);
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 8);
+            mbar_init(&x_ready[i], 4);
         }
         mbar_init(w_full, 1);
         *abort_flag = 0;
@@ -150,6 +167,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t* ones = reinterpret_cast<uint32_t*>(smem + L.off_ones);
         for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
             ones[i] = ((i < 512) && ((i & 3) == 0)) ? one : 0u;
+        }
+        if constexpr (kLn) {
+            float* gb = reinterpret_cast<float*>(smem + L.off_ln);
+            for (int i = threadIdx.x; i < K; i += blockDim.x) {
+                gb[i] = ln.gamma[i];
+                gb[kMaxK + i] = ln.beta[i];
+            }
         }
         fence_proxy_async_smem();
     }
@@ -173,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_3d(smem + L.off_wg + a * L.kb * 128, &tm_wg, w_full, a * 64, 0, 0);
             }
             const int panels = (K + 63) / 64;
-            for (int i = 0; i < n_mine; ++i) {
+            for (int i = 0; i < (kLn ? 0 : n_mine); ++i) {
                 const int mt = blockIdx.x + i * gridDim.x;
                 const int s = i % L.xs;
                 if (i >= L.xs && !mbar_wait(&x_empty[s], ((i / L.xs) - 1) & 1, abort_flag)) {
@@ -199,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t chunk_ctr = 0;
             for (int i = 0; i < n_mine; ++i) {
                 const int s = i % L.xs;
-                if (!mbar_wait_w(&x_full[s], (i / L.xs) & 1, abort_flag)) {
+                if (!mbar_wait_w(kLn ? &x_ready[s] : &x_full[s], (i / L.xs) & 1, abort_flag)) {
                     goto done;
                 }
                 tc_fence_after();
@@ -226,6 +250,116 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_commit_w(&acc_full[bf]);
                 }
                 umma_commit_w(&x_empty[s]);
+            }
+        }
+    } else if (kLn && warp > kMmaWarp) {
+        // LayerNorm warpgroup: thread r normalises row r of each tile into the x stage
+        const int r = static_cast<int>(threadIdx.x) - 32 * (kMmaWarp + 1);
+        const int nchk = K / 8; // 16-byte chunks of a row
+        const float* gam = reinterpret_cast<const float*>(smem + L.off_ln);
+        const float* bet = gam + kMaxK;
+        const float inv_k = 1.0f / static_cast<float>(K);
+        uint4 zr[kMaxK / 8];
+        auto load_row = [&](int i) {
+            const int row = (static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x)) * 128 + r;
+            const uint16_t* src = ln.z + static_cast<int64_t>(row) * K;
+#pragma unroll
+            for (int c = 0; c < kMaxK / 8; ++c) {
+                zr[c] = (c < nchk && row < M) ? ld_global_stream_v4(src + 8 * c)
+                                              : make_uint4(0u, 0u, 0u, 0u);
+            }
+        };
+        if (n_mine > 0) {
+            load_row(0);
+        }
+        for (int i = 0; i < n_mine; ++i) {
+            const int s = i % L.xs;
+            const int row = (static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x)) * 128 + r;
+            // two passes over the row in registers: mean, then the centred sum of squares
+            // (f32x2 partial sums in two chains each, so the adds overlap)
+            float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+            for (int c = 0; c < kMaxK / 8; ++c) {
+                if (c < nchk) {
+                    const uint32_t w4[4] = {zr[c].x, zr[c].y, zr[c].z, zr[c].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        s2[e & 1] = fadd2(s2[e & 1], E::to_float2(w4[e]));
+                    }
+                }
+            }
+            const float mean = ((s2[0].x + s2[0].y) + (s2[1].x + s2[1].y)) * inv_k;
+            const float2 nm2 = make_float2(-mean, -mean);
+            float2 q2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+            for (int c = 0; c < kMaxK / 8; ++c) {
+                if (c < nchk) {
+                    const uint32_t w4[4] = {zr[c].x, zr[c].y, zr[c].z, zr[c].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 d = fadd2(E::to_float2(w4[e]), nm2);
+                        q2[e & 1] = ffma2(d, d, q2[e & 1]);
+                    }
+                }
+            }
+            const float rstd =
+                rsqrtf(((q2[0].x + q2[0].y) + (q2[1].x + q2[1].y)) * inv_k + ln.eps);
+            // y = (x - mean) rstd gamma + beta = t gamma + beta with t = x rstd - mean rstd;
+            // the packed result replaces z, before waiting for the stage
+            const float2 r2 = make_float2(rstd, rstd);
+            const float2 mr2 = make_float2(-mean * rstd, -mean * rstd);
+#pragma unroll
+            for (int c = 0; c < kMaxK / 8; ++c) {
+                if (c < nchk) {
+                    const uint32_t w4[4] = {zr[c].x, zr[c].y, zr[c].z, zr[c].w};
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int k0 = 8 * c + 2 * e;
+                        const float2 t = ffma2(E::to_float2(w4[e]), r2, mr2);
+                        const float2 yv = ffma2(t, make_float2(gam[k0], gam[k0 + 1]),
+                                                make_float2(bet[k0], bet[k0 + 1]));
+                        o[e] = E::pack(yv.x, yv.y);
+                    }
+                    zr[c] = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+            if (row < M) {
+                if (ln.mean) {
+                    ln.mean[row] = mean;
+                }
+                if (ln.rstd) {
+                    ln.rstd[row] = rstd;
+                }
+            }
+            // the z row of the tile after next into L2 (its load below is then an L2 hit)
+            if (i + 2 < n_mine) {
+                const int row2 = row + 2 * static_cast<int>(gridDim.x) * 128;
+                if (row2 < M) {
+                    for (int c = 0; c < nchk; c += 8) {
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(ln.z + static_cast<int64_t>(row2) * K + 8 * c));
+                    }
+                }
+            }
+            // the MMAs of the tile that used this stage last are done
+            if (i >= L.xs && !mbar_wait(&x_empty[s], ((i / L.xs) - 1) & 1, abort_flag)) {
+                goto done;
+            }
+            const uint32_t xrow = sbase + L.off_x + s * L.x_stage + r * 128;
+#pragma unroll
+            for (int c = 0; c < kMaxK / 8; ++c) {
+                if (c < nchk) {
+                    // chunk c: panel c / 8, 16-byte chunk c % 8 of the row (128-byte swizzle)
+                    attn::sts128(xrow + (c >> 3) * 16384 + ((((c & 7) ^ (r & 7))) << 4), zr[c]);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&x_ready[s]);
+            }
+            if (i + 1 < n_mine) {
+                load_row(i + 1); // in flight while the MMAs of this tile run
             }
         }
     } else {
@@ -357,14 +491,24 @@ __global__ void gdp_fwd_generic_kernel(const uint16_t* __restrict__ x,
     }
 }
 
+bool fwd_fast_shape(int K, int N) {
+    const FwdLayout L = fwd_layout(K, N);
+    return (K % 16 == 0) && K >= 16 && K <= kMaxK && 2 * L.kb * L.npad * 2 <= kWeightBudget &&
+           L.total <= 227 * 1024;
+}
+
+// ln != nullptr: x is LayerNorm(ln->z) and only the fused tcgen05 kernel may be used (the
+// caller takes the two-kernel route for other shapes).
 template <typename T>
 int gdp_fwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const void* wp,
                  const void* bp, const void* wg, const void* bg, const void* mask, void* out,
-                 int M, int K, int N) {
+                 int M, int K, int N, const LnIn* ln = nullptr) {
     const FwdLayout L = fwd_layout(K, N);
-    const bool fast = (K % 16 == 0) && K >= 16 && K <= kMaxK &&
-                      2 * L.kb * L.npad * 2 <= kWeightBudget && aligned16(x) && aligned16(wp) &&
-                      aligned16(wg) && aligned16(out) && L.total <= 227 * 1024;
+    const bool fast = fwd_fast_shape(K, N) && aligned16(ln ? ln->z : x) && aligned16(wp) &&
+                      aligned16(wg) && aligned16(out);
+    if (ln && !fast) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "gdp_fwd: fused LayerNorm needs the tcgen05 shape");
+    }
     if (!fast) {
         dim3 block(16, 16), grid((N + 15) / 16, (M + 15) / 16);
         gdp_fwd_generic_kernel<T><<<grid, block, 0, st>>>(
@@ -377,20 +521,22 @@ int gdp_fwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const vo
     CUtensorMap tx, twp, twg, tout;
     // x [M, K]: dims (K, M, 1), box 64 x 128; weights [K, N]: dims (N, K, 1), box 64 x K;
     // out [M, N]: dims (N, M, 1), box 64 x 128 (stores)
-    CFK_TRY(make_tmap_3d(&tx, x, K, M, 1, 2ull * K, 2ull * K * M, 64, 128, 1, 128, "gdp x"));
+    CFK_TRY(make_tmap_3d(&tx, ln ? ln->z : x, K, M, 1, 2ull * K, 2ull * K * M, 64, 128, 1, 128,
+                         "gdp x"));
     CFK_TRY(make_tmap_3d(&twp, wp, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wp"));
     CFK_TRY(make_tmap_3d(&twg, wg, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wg"));
     CFK_TRY(make_tmap_3d(&tout, out, N, M, 1, 2ull * N, 2ull * N * M, 64, 128, 1, 128,
                          "gdp out"));
-    auto kern = gdp_fwd_kernel<T>;
+    auto kern = ln ? gdp_fwd_kernel<T, true> : gdp_fwd_kernel<T, false>;
     CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
-                             "gdp_fwd"));
+                             ln ? "gdp_fwd_ln" : "gdp_fwd"));
     const int n_mt = (M + 127) / 128;
     const int grid = std::min(n_mt, dev.num_sms);
-    kern<<<grid, kThreads, L.total, st>>>(tx, twp, twg, tout, static_cast<const uint16_t*>(bp),
-                                          static_cast<const uint16_t*>(bg),
-                                          static_cast<const uint16_t*>(mask), M, K, N);
-    return check_launch("gdp_fwd");
+    const LnIn none{};
+    kern<<<grid, ln ? kThreads + 128 : kThreads, L.total, st>>>(
+        tx, twp, twg, tout, static_cast<const uint16_t*>(bp), static_cast<const uint16_t*>(bg),
+        static_cast<const uint16_t*>(mask), M, K, N, ln ? *ln : none);
+    return check_launch(ln ? "gdp_fwd_ln" : "gdp_fwd");
 }
 
 // ==========================================================================================
@@ -1719,6 +1865,63 @@ extern "C" int cfk_gdp_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, 
     return dtype == CFK_BF16
                ? gdp::gdp_fwd_impl<__nv_bfloat16>(st, dev, x, wp, bp, wg, bg, mask, out, m, k, n)
                : gdp::gdp_fwd_impl<__half>(st, dev, x, wp, bp, wg, bg, mask, out, m, k, n);
+}
+
+extern "C" int cfk_ln_gdp_fwd_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes) {
+    clear_error();
+    CFK_TRY(check_gdp_args("cfk_ln_gdp_fwd_workspace_size", CFK_BF16, M, K, N));
+    if (!bytes) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_ln_gdp_fwd_workspace_size: null pointer");
+    }
+    // the fused kernel needs none; other shapes stage LayerNorm(z) [M, K] in the workspace
+    *bytes = gdp::fwd_fast_shape(static_cast<int>(K), static_cast<int>(N))
+                 ? 0
+                 : static_cast<size_t>(M) * static_cast<size_t>(K) * 2;
+    return CFK_OK;
+}
+
+extern "C" int cfk_ln_gdp_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* z,
+                              const float* gamma, const float* beta, float eps, const void* wp,
+                              const void* bp, const void* wg, const void* bg, const void* mask,
+                              void* out, float* mean, float* rstd, void* workspace,
+                              size_t workspace_bytes, int64_t M, int64_t K, int64_t N) {
+    clear_error();
+    CFK_TRY(check_gdp_args("cfk_ln_gdp_fwd", dtype, M, K, N));
+    if (!(eps >= 0.f)) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_ln_gdp_fwd: eps must be >= 0");
+    }
+    if (M == 0) {
+        return CFK_OK;
+    }
+    if (!z || !gamma || !beta || !wp || !bp || !wg || !bg || !mask || !out) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_ln_gdp_fwd: null buffer");
+    }
+    DeviceInfo dev;
+    CFK_TRY(current_device(&dev));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int m = static_cast<int>(M), k = static_cast<int>(K), n = static_cast<int>(N);
+    const bool fused = gdp::fwd_fast_shape(k, n) && aligned16(z) && aligned16(wp) &&
+                       aligned16(wg) && aligned16(out);
+    if (fused) {
+        const gdp::LnIn ln{static_cast<const uint16_t*>(z), gamma, beta, mean, rstd, eps};
+        return dtype == CFK_BF16 ? gdp::gdp_fwd_impl<__nv_bfloat16>(st, dev, nullptr, wp, bp, wg,
+                                                                     bg, mask, out, m, k, n, &ln)
+                                 : gdp::gdp_fwd_impl<__half>(st, dev, nullptr, wp, bp, wg, bg,
+                                                             mask, out, m, k, n, &ln);
+    }
+    // two kernels through a staged LayerNorm output
+    const size_t need = static_cast<size_t>(M) * static_cast<size_t>(K) * 2;
+    if (!workspace || workspace_bytes < need || !aligned16(workspace)) {
+        return fail(CFK_ERR_INVALID_ARGUMENT,
+                    "cfk_ln_gdp_fwd: this shape or alignment needs a 16-byte aligned %zu-byte "
+                    "workspace (got %zu)", need, workspace_bytes);
+    }
+    CFK_TRY(cfk_ln_fwd(stream, dtype, z, gamma, beta, workspace, mean, rstd, M, K, eps));
+    clear_error();
+    return dtype == CFK_BF16 ? gdp::gdp_fwd_impl<__nv_bfloat16>(st, dev, workspace, wp, bp, wg,
+                                                                 bg, mask, out, m, k, n)
+                             : gdp::gdp_fwd_impl<__half>(st, dev, workspace, wp, bp, wg, bg,
+                                                         mask, out, m, k, n);
 }
 
 extern "C" int cfk_gdp_bwd_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes) {

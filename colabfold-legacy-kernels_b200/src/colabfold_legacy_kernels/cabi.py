@@ -56,6 +56,9 @@ SIGNATURES = {
     "cfk_ln_bwd_noalloc": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
                            _f32],
     "cfk_gdp_fwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64],
+    "cfk_ln_gdp_fwd_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
+    "cfk_ln_gdp_fwd": [_vp, _int, _vp, _vp, _vp, _f32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                       _vp, _sz, _i64, _i64, _i64],
     "cfk_gdp_bwd_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
     "cfk_gdp_bwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                     _vp, _sz, _i64, _i64, _i64],

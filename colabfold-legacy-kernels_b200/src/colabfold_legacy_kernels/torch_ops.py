@@ -128,6 +128,29 @@ def gdp_fwd(x, wp, bp, wg, bg, mask, out=None):
     return out
 
 
+def ln_gdp_fwd(z, gamma, beta, eps, wp, bp, wg, bg, mask, out=None, return_stats=False,
+               workspace=None):
+    """gdp_fwd(layer_norm_fwd(z, gamma, beta, eps), wp, bp, wg, bg, mask) in one kernel where the
+    shape allows (cfk_ln_gdp_fwd); with return_stats also the LayerNorm mean and rstd."""
+    _check(z, gamma, beta, wp, bp, wg, bg, mask)
+    m, k = z.shape
+    n = wp.shape[1]
+    if out is None:
+        out = torch.empty((m, n), dtype=z.dtype, device=z.device)
+    mean = rstd = None
+    if return_stats:
+        mean = torch.empty(m, dtype=torch.float32, device=z.device)
+        rstd = torch.empty(m, dtype=torch.float32, device=z.device)
+    if workspace is None:
+        nbytes = cabi.workspace_size("cfk_ln_gdp_fwd_workspace_size", m, k, n)
+        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=z.device)
+    with torch.cuda.device(z.device):
+        cabi.call("cfk_ln_gdp_fwd", _stream(z.device), _dtype_code(z), _ptr(z), _ptr(gamma),
+                  _ptr(beta), float(eps), _ptr(wp), _ptr(bp), _ptr(wg), _ptr(bg), _ptr(mask),
+                  _ptr(out), _ptr(mean), _ptr(rstd), _ptr(workspace), workspace.numel(), m, k, n)
+    return (out, mean, rstd) if return_stats else out
+
+
 def gdp_bwd(x, wp, bp, wg, bg, mask, dout, workspace=None):
     """(dx, dwp, dbp, dwg, dbg); weight and bias gradients in f32."""
     _check(x, wp, bp, wg, bg, mask, dout)

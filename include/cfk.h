@@ -147,6 +147,18 @@ CFK_API int cfk_gdp_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, con
                 const void* bp, const void* wg, const void* bg, const void* mask, void* out,
                 int64_t M, int64_t K, int64_t N);
 
+/* LayerNorm fused into the forward (no counterpart in the reference; the two-step
+ * x = LayerNorm(z) (cuda/volta_ops.cu:28-60) then VoltaGdp of triangle multiplication):
+ * out = gdp(LayerNorm(z; gamma, beta, eps)) without writing x to memory.  z [M,K] in dtype,
+ * gamma, beta f32 [K]; mean, rstd (f32 [M]) may be NULL.  Shapes outside the tcgen05 path
+ * (cfk_ln_gdp_fwd_workspace_size reports a nonzero size for them) stage x in the workspace. */
+CFK_API int cfk_ln_gdp_fwd_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes);
+CFK_API int cfk_ln_gdp_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* z, const float* gamma,
+                   const float* beta, float eps, const void* wp, const void* bp,
+                   const void* wg, const void* bg, const void* mask, void* out, float* mean,
+                   float* rstd, void* workspace, size_t workspace_bytes, int64_t M, int64_t K,
+                   int64_t N);
+
 /* Bytes of scratch memory cfk_gdp_bwd needs. */
 CFK_API int cfk_gdp_bwd_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes);
 

@@ -71,3 +71,33 @@ def test_gdp_triangle_multiplication_shape(cuda_device):
     for a, b, name in ((dwp, r[1], "dwp"), (dbp, r[2], "dbp"), (dwg, r[3], "dwg"),
                        (dbg, r[4], "dbg")):
         assert_close_f32(a, b, name)
+
+
+LN_GDP_SHAPES = [(1000, 128, 256), (300, 64, 64), (257, 48, 200), (130, 128, 512), (77, 40, 24),
+                 (64, 16, 8)]
+
+
+@pytest.mark.parametrize("m,k,n", LN_GDP_SHAPES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_ln_gdp_fwd(cuda_device, m, k, n, dtype):
+    """cfk_ln_gdp_fwd = gdp_fwd(LayerNorm(z)): fused kernel for the tcgen05 shapes, LayerNorm
+    staged in the workspace for the others (K = 40, N = 512 here)."""
+    from colabfold_legacy_kernels import torch_ops
+    g = torch.Generator().manual_seed(3 * m + k + n)
+    z = (2.0 * torch.randn(m, k, generator=g) + 0.5).to(dtype)
+    gamma = 1.0 + 0.1 * torch.randn(k, generator=g)
+    beta = 0.1 * torch.randn(k, generator=g)
+    _, wp, bp, wg, bg, mask, _ = _inputs(m, k, n, dtype, seed=m + 2 * k + n)
+    out, mean, rstd = torch_ops.ln_gdp_fwd(z.cuda(), gamma.cuda(), beta.cuda(), 1e-5, wp, bp, wg,
+                                           bg, mask, return_stats=True)
+    torch.cuda.synchronize()
+    x, rmean, rrstd = oracle.layer_norm_fwd(z, gamma, beta, 1e-5)
+    ref = oracle.gdp_fwd(x.to(dtype), *(t.cpu() for t in (wp, bp, wg, bg, mask)))
+    assert_close_bf16(out, ref, "out")
+    assert_close_f32(mean, rmean, "mean")
+    assert_close_f32(rstd, rrstd, "rstd")
+    # the same result as the two separate kernels, up to the 16-bit rounding of x
+    y = torch_ops.layer_norm_fwd(z.cuda(), gamma.cuda(), beta.cuda(), 1e-5)
+    two = torch_ops.gdp_fwd(y, wp, bp, wg, bg, mask)
+    torch.cuda.synchronize()
+    assert_close_bf16(out, two, "out vs LayerNorm then GDP", rtol=1e-2, atol=1e-2)
