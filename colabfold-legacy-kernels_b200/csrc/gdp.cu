@@ -200,6 +200,13 @@ __global__ void __launch_bounds__(kLn ? kThreads + 128 : kThreads, 1)
             for (int i = 0; i < (kLn ? 0 : n_mine); ++i) {
                 const int mt = blockIdx.x + i * gridDim.x;
                 const int s = i % L.xs;
+                // the x tiles two and three ahead into L2: with one x stage beside the weights,
+                // each load is issued only once the previous tile's MMAs are done
+                for (int ip = (i == 0 ? 1 : i + 3); ip <= i + 3 && ip < n_mine; ++ip) {
+                    for (int pn = 0; pn < panels; ++pn) {
+                        tma_prefetch_l2_3d(&tm_x, pn * 64, (blockIdx.x + ip * gridDim.x) * 128, 0);
+                    }
+                }
                 if (i >= L.xs && !mbar_wait(&x_empty[s], ((i / L.xs) - 1) & 1, abort_flag)) {
                     goto done;
                 }
