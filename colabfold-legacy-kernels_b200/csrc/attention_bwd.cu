@@ -355,28 +355,26 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             __syncwarp();
             tc_fence_after();
             const uint32_t part = tmem + lane_off + C::kPartBase + pb * 3 * G::kDp + w * G::kDp;
+            {
+                // the whole partial with one wait, and the buffer released before the stores
+                uint32_t raw[D];
 #pragma unroll
-            for (int c0 = 0; c0 < D; c0 += 16) {
-                constexpr int kN = D < 16 ? D : 16;
-                uint32_t raw[kN];
-                if constexpr (kN == 8) {
-                    tmem_ld8(part + c0, raw);
-                } else {
-                    tmem_ld16(part + c0, raw);
+                for (int c0 = 0; c0 < D; c0 += 8) {
+                    tmem_ld8(part + c0, *reinterpret_cast<uint32_t (*)[8]>(&raw[c0]));
                 }
                 tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&part_empty[pb]);
+                }
 #pragma unroll
-                for (int q = 0; q < kN / 4; ++q) {
-                    const int col = c0 + q * 4;
+                for (int q = 0; q < D / 4; ++q) {
+                    const int col = q * 4;
                     sts128(stg + (col / C::kPW) * C::kPanelBytes +
                                stg_chunk<C::kRowB>(jl, (col % C::kPW) / 4),
                            make_uint4(raw[4 * q], raw[4 * q + 1], raw[4 * q + 2], raw[4 * q + 3]));
                 }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&part_empty[pb]);
             }
             fence_proxy_async_smem();
             named_bar_sync(1 + w, 128);
