@@ -95,6 +95,14 @@ def test_fwd_triangle_shape(cuda_device):
     _check(t["q"], t["k"], t["v"], t["bias"], t["kmask"], t["scale"], "triangle")
 
 
+def test_fwd_large_complex_shape(cuda_device):
+    """Config C5's shape class (N_res = 2048: 16 key tiles per row, all-ones mask), two rows."""
+    cfg = oracle.configs.scaled(oracle.configs.C5, n=2)
+    inp = oracle.configs.make_attention_inputs(cfg, device="cpu")
+    t = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in inp.items()}
+    _check(t["q"], t["k"], t["v"], t["bias"], t["kmask"], t["scale"], "tri-2048")
+
+
 def test_fwd_deterministic_and_no_timeouts(cuda_device):
     from colabfold_legacy_kernels import cabi
     cabi.clear_device_status()
