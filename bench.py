@@ -448,7 +448,69 @@ def run_ours(args, rank, world, local_rank):
     if world == 1 and not args.skip_extras:
         result["layernorm"] = bench_layernorm(dev, pk)
         result["gdp"] = bench_gdp(dev, pk)
+    elif not args.skip_extras:
+        result.update(bench_ln_gdp_sharded(dev, pk, world))
     return result
+
+
+def bench_ln_gdp_sharded(dev, pk, world, steps=20):
+    """LayerNorm and GDP on config C4 with its rows sharded over the N ranks (ShardedLnGdp: the
+    forwards are row-local, each backward ends with one all-reduce of the parameter gradients).
+    Whole-job rates: C4's algorithmic bytes / flops over the slowest rank's time."""
+    import torch
+    import torch.distributed as dist
+    import oracle
+    from colabfold_legacy_kernels import torch_ops
+    from colabfold_legacy_kernels.parallel import ShardedLnGdp
+    inp = oracle.configs.make_ln_gdp_inputs(oracle.configs.C4, device=dev)
+    m, c = inp["x"].shape
+    n = inp["wp"].shape[1]
+    sh = ShardedLnGdp()
+    m0, m1 = sh.rows(m)
+    x, dy, mask, dout = (inp[k][m0:m1].contiguous() for k in ("x", "dy", "mask", "dout"))
+    gamma, beta, wp, bp, wg, bg = (inp[k] for k in ("gamma", "beta", "wp", "bp", "wg", "bg"))
+    del inp
+
+    def slowest(ms):
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    y, mean, rstd = torch_ops.layer_norm_fwd(x, gamma, beta, 1e-5, return_stats=True)
+    out = torch.empty((m1 - m0, n), dtype=x.dtype, device=dev)
+    ms = {"ln_fwd": slowest(_stream_ms(lambda: torch_ops.layer_norm_fwd(x, gamma, beta, 1e-5,
+                                                                        out=y), steps)),
+          "ln_bwd": slowest(_stream_ms(lambda: sh.layer_norm_bwd(x, gamma, dy, 1e-5, mean, rstd),
+                                       steps)),
+          "gdp_fwd": slowest(_stream_ms(lambda: torch_ops.gdp_fwd(x, wp, bp, wg, bg, mask,
+                                                                  out=out), steps)),
+          "gdp_bwd": slowest(_stream_ms(lambda: sh.gdp_bwd(x, wp, bp, wg, bg, mask, dout),
+                                        steps))}
+    note = ("rows sharded over %d GPUs; backward parameter gradients all-reduced once (NCCL); "
+            "inputs larger than L2, launches back to back" % world)
+
+    def gbs(nbytes, t):
+        return nbytes / (t * 1e-3) / 1e9
+
+    def tfs(flops, t):
+        return flops / (t * 1e-3) / 1e12
+
+    return {
+        "layernorm": {"sharding": note, "n_gpus": world,
+                      "fwd": {"metric": "LayerNorm fwd HBM GB/s [1M x 128] bf16", "unit": "GB/s",
+                              "value": gbs(oracle.layer_norm.bytes_fwd(m, c), ms["ln_fwd"]),
+                              "ms": ms["ln_fwd"]},
+                      "bwd": {"metric": "LayerNorm bwd HBM GB/s [1M x 128] bf16", "unit": "GB/s",
+                              "value": gbs(oracle.layer_norm.bytes_bwd(m, c), ms["ln_bwd"]),
+                              "ms": ms["ln_bwd"]}},
+        "gdp": {"sharding": note, "n_gpus": world,
+                "fwd": {"metric": "GDP fwd TFLOP/s [1M x 128 -> 256] bf16", "unit": "TFLOP/s",
+                        "value": tfs(oracle.gdp.flops_fwd(m, c, n), ms["gdp_fwd"]),
+                        "ms": ms["gdp_fwd"]},
+                "bwd": {"metric": "GDP bwd TFLOP/s [1M x 128 -> 256] bf16", "unit": "TFLOP/s",
+                        "value": tfs(oracle.gdp.flops_bwd(m, c, n), ms["gdp_bwd"]),
+                        "ms": ms["gdp_bwd"]}},
+    }
 
 
 L2_NOTE = "inputs larger than L2 (x 268 MB), launches back to back, no flush"

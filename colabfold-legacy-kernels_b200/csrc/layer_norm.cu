@@ -96,7 +96,7 @@ __global__ __launch_bounds__(kThreads) void ln_fwd_vec_kernel(
 #pragma unroll
             for (int e = 0; e < NV * 8; ++e) {
                 const float d = xv[e] - mean;
-                q += d * d;
+                q = __fmaf_rn(d, d, q);
             }
             const float var = group_sum<LPR>(q) * (1.0f / C);
             const float rstd = rsqrtf(var + eps);
@@ -107,8 +107,12 @@ __global__ __launch_bounds__(kThreads) void ln_fwd_vec_kernel(
 #pragma unroll
                     for (int p = 0; p < 4; ++p) {
                         const int e0 = v * 8 + 2 * p;
-                        const float y0 = (xv[e0] - mean) * rstd * gm[e0] + bt[e0];
-                        const float y1 = (xv[e0 + 1] - mean) * rstd * gm[e0 + 1] + bt[e0 + 1];
+                        // explicit roundings: every unrolled row group evaluates the same
+                        // operations, so a row's result does not depend on its place in the call
+                        const float y0 = __fmaf_rn(__fmul_rn(__fsub_rn(xv[e0], mean), rstd),
+                                                   gm[e0], bt[e0]);
+                        const float y1 = __fmaf_rn(__fmul_rn(__fsub_rn(xv[e0 + 1], mean), rstd),
+                                                   gm[e0 + 1], bt[e0 + 1]);
                         w[p] = E::pack(y0, y1);
                     }
                     st_global_v4(y + row * C + (v * LPR + gl) * 8, make_uint4(w[0], w[1], w[2], w[3]));
@@ -149,7 +153,7 @@ __global__ __launch_bounds__(kThreads) void ln_fwd_generic_kernel(
         float q = 0.f;
         for (int c = lane; c < C; c += 32) {
             const float d = E::to_float(xr[c]) - mean;
-            q += d * d;
+            q = __fmaf_rn(d, d, q);
         }
         const float rstd = rsqrtf(group_sum<32>(q) / C + eps);
         for (int c = lane; c < C; c += 32) {
@@ -243,7 +247,7 @@ __global__ __launch_bounds__(kThreads) void ln_bwd_vec_kernel(
 #pragma unroll
                 for (int e = 0; e < NV * 8; ++e) {
                     const float d = xv[e] - mean;
-                    q += d * d;
+                    q = __fmaf_rn(d, d, q);
                 }
                 rstd = rsqrtf(group_sum<LPR>(q) * (1.0f / C) + eps);
             }
@@ -251,11 +255,11 @@ __global__ __launch_bounds__(kThreads) void ln_bwd_vec_kernel(
             float sg = 0.f, sgx = 0.f;
 #pragma unroll
             for (int e = 0; e < NV * 8; ++e) {
-                const float xh = (xv[e] - mean) * rstd;
-                const float gg = dv[e] * gm[e];
+                const float xh = __fmul_rn(__fsub_rn(xv[e], mean), rstd);
+                const float gg = __fmul_rn(dv[e], gm[e]);
                 xv[e] = xh;
                 sg += gg;
-                sgx += gg * xh;
+                sgx = __fmaf_rn(gg, xh, sgx);
             }
             sg = group_sum<LPR>(sg) * (1.0f / C);
             sgx = group_sum<LPR>(sgx) * (1.0f / C);
@@ -266,15 +270,20 @@ __global__ __launch_bounds__(kThreads) void ln_bwd_vec_kernel(
 #pragma unroll
                     for (int p = 0; p < 4; ++p) {
                         const int e0 = v * 8 + 2 * p;
-                        const float d0 = rstd * (dv[e0] * gm[e0] - sg - xv[e0] * sgx);
-                        const float d1 = rstd * (dv[e0 + 1] * gm[e0 + 1] - sg - xv[e0 + 1] * sgx);
+                        // explicit roundings (see the forward)
+                        const float d0 = __fmul_rn(
+                            rstd, __fmaf_rn(-xv[e0], sgx,
+                                            __fsub_rn(__fmul_rn(dv[e0], gm[e0]), sg)));
+                        const float d1 = __fmul_rn(
+                            rstd, __fmaf_rn(-xv[e0 + 1], sgx,
+                                            __fsub_rn(__fmul_rn(dv[e0 + 1], gm[e0 + 1]), sg)));
                         w[p] = E::pack(d0, d1);
                     }
                     st_global_v4(dx + row * C + (v * LPR + gl) * 8, make_uint4(w[0], w[1], w[2], w[3]));
                 }
 #pragma unroll
                 for (int e = 0; e < NV * 8; ++e) {
-                    dg[e] += dv[e] * xv[e];
+                    dg[e] = __fmaf_rn(dv[e], xv[e], dg[e]);
                     db[e] += dv[e];
                 }
             }
@@ -354,7 +363,7 @@ __global__ __launch_bounds__(kThreads) void ln_bwd_generic_kernel(
             float q = 0.f;
             for (int c = lane; c < C; c += 32) {
                 const float d = E::to_float(xr[c]) - mean;
-                q += d * d;
+                q = __fmaf_rn(d, d, q);
             }
             rstd = rsqrtf(group_sum<32>(q) / C + eps);
         }

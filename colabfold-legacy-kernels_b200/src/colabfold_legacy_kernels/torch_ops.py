@@ -98,13 +98,21 @@ def layer_norm_fwd(x, gamma, beta, eps, return_stats=False, out=None):
     return (y, mean, rstd) if return_stats else y
 
 
-def layer_norm_bwd(x, gamma, dy, eps, mean=None, rstd=None, workspace=None):
-    """(dx, dgamma, dbeta); mean/rstd from layer_norm_fwd(return_stats=True) or recomputed."""
+def layer_norm_bwd(x, gamma, dy, eps, mean=None, rstd=None, workspace=None, grads=None):
+    """(dx, dgamma, dbeta); mean/rstd from layer_norm_fwd(return_stats=True) or recomputed.
+    `grads` = (dx, dgamma, dbeta) preallocated (contiguous; dgamma, dbeta f32 [C]) or None."""
     _check(x, gamma, dy, mean, rstd)
     m, c = x.shape
-    dx = torch.empty_like(x)
-    dgamma = torch.empty(c, dtype=torch.float32, device=x.device)
-    dbeta = torch.empty(c, dtype=torch.float32, device=x.device)
+    if grads is None:
+        dx = torch.empty_like(x)
+        dgamma = torch.empty(c, dtype=torch.float32, device=x.device)
+        dbeta = torch.empty(c, dtype=torch.float32, device=x.device)
+    else:
+        dx, dgamma, dbeta = grads
+        _check(dx, dgamma, dbeta)
+        if dx.shape != x.shape or dgamma.shape != (c,) or dbeta.shape != (c,) or \
+                dgamma.dtype != torch.float32 or dbeta.dtype != torch.float32:
+            raise ValueError("grads must be dx like x and f32 dgamma, dbeta of shape [C]")
     if workspace is None:
         nbytes = cabi.workspace_size("cfk_ln_bwd_workspace_size", m, c)
         workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x.device)
@@ -151,16 +159,25 @@ def ln_gdp_fwd(z, gamma, beta, eps, wp, bp, wg, bg, mask, out=None, return_stats
     return (out, mean, rstd) if return_stats else out
 
 
-def gdp_bwd(x, wp, bp, wg, bg, mask, dout, workspace=None):
-    """(dx, dwp, dbp, dwg, dbg); weight and bias gradients in f32."""
+def gdp_bwd(x, wp, bp, wg, bg, mask, dout, workspace=None, grads=None):
+    """(dx, dwp, dbp, dwg, dbg); weight and bias gradients in f32.  `grads` = those five
+    preallocated (contiguous; f32 [K,N], [N], [K,N], [N] for the parameter gradients) or None."""
     _check(x, wp, bp, wg, bg, mask, dout)
     m, k = x.shape
     n = wp.shape[1]
-    dx = torch.empty_like(x)
-    dwp = torch.empty((k, n), dtype=torch.float32, device=x.device)
-    dwg = torch.empty((k, n), dtype=torch.float32, device=x.device)
-    dbp = torch.empty(n, dtype=torch.float32, device=x.device)
-    dbg = torch.empty(n, dtype=torch.float32, device=x.device)
+    if grads is None:
+        dx = torch.empty_like(x)
+        dwp = torch.empty((k, n), dtype=torch.float32, device=x.device)
+        dwg = torch.empty((k, n), dtype=torch.float32, device=x.device)
+        dbp = torch.empty(n, dtype=torch.float32, device=x.device)
+        dbg = torch.empty(n, dtype=torch.float32, device=x.device)
+    else:
+        dx, dwp, dbp, dwg, dbg = grads
+        _check(dx, dwp, dbp, dwg, dbg)
+        if dx.shape != x.shape or dwp.shape != (k, n) or dwg.shape != (k, n) or \
+                dbp.shape != (n,) or dbg.shape != (n,) or \
+                any(t.dtype != torch.float32 for t in (dwp, dbp, dwg, dbg)):
+            raise ValueError("grads must be dx like x and f32 dwp, dbp, dwg, dbg")
     if workspace is None:
         nbytes = cabi.workspace_size("cfk_gdp_bwd_workspace_size", m, k, n)
         workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x.device)

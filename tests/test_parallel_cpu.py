@@ -114,3 +114,76 @@ def test_failed_rank_gives_error_not_hang():
     assert results[1][0] == "error" and "injected" in results[1][1]
     # the surviving rank's all-reduce ends with an error (peer gone), within the timeout
     assert results[0][0] == "error", results[0]
+
+
+# --------------------------------------------------------------------------------------------
+# LayerNorm and GDP rows sharded, parameter gradients all-reduced (ShardedLnGdp)
+# --------------------------------------------------------------------------------------------
+def _ln_gdp_inputs():
+    g = torch.Generator().manual_seed(5)
+    m, c, n = 11, 16, 24
+    x = torch.randn(m, c, generator=g, dtype=torch.float64)
+    gamma = 1 + 0.1 * torch.randn(c, generator=g, dtype=torch.float64)
+    dy = torch.randn(m, c, generator=g, dtype=torch.float64)
+    wp, wg = (torch.randn(c, n, generator=g, dtype=torch.float64) / 4 for _ in range(2))
+    bp, bg = (0.3 * torch.randn(n, generator=g, dtype=torch.float64) for _ in range(2))
+    mask = (torch.rand(m, generator=g) > 0.2).to(torch.float64)
+    dout = torch.randn(m, n, generator=g, dtype=torch.float64)
+    return x, gamma, dy, wp, bp, wg, bg, mask, dout
+
+
+def _ln_gdp_worker(rank, world, port, queue):
+    try:
+        sys.path[:0] = [REPO, os.path.join(REPO, "colabfold-legacy-kernels_b200", "src")]
+        import torch.distributed as dist
+        import oracle
+        from colabfold_legacy_kernels.parallel import ShardedLnGdp
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank,
+                                world_size=world, timeout=timedelta(seconds=15))
+        x, gamma, dy, wp, bp, wg, bg, mask, dout = _ln_gdp_inputs()
+
+        def ln_bwd(x, gamma, dy, eps, mean, rstd, grads):
+            for t, v in zip(grads, oracle.layer_norm_bwd(x, gamma, dy, eps)):
+                t.copy_(v)
+
+        def gdp_bwd(x, wp, bp, wg, bg, mask, dout, grads):
+            for t, v in zip(grads, oracle.gdp_bwd(x, wp, bp, wg, bg, mask, dout)):
+                t.copy_(v)
+
+        sh = ShardedLnGdp(ln_bwd=ln_bwd, gdp_bwd=gdp_bwd)
+        r0, r1 = sh.rows(x.shape[0])
+        ln = sh.layer_norm_bwd(x[r0:r1], gamma, dy[r0:r1], 1e-5)
+        gd = sh.gdp_bwd(x[r0:r1], wp, bp, wg, bg, mask[r0:r1], dout[r0:r1])
+        ln_ref = oracle.layer_norm_bwd(x, gamma, dy, 1e-5)
+        gd_ref = oracle.gdp_bwd(x, wp, bp, wg, bg, mask, dout)
+        errs = {"ln_dx": float((ln[0].double() - ln_ref[0][r0:r1]).abs().max())}
+        for name, a, b in (("dgamma", ln[1], ln_ref[1]), ("dbeta", ln[2], ln_ref[2])):
+            errs[name] = float((a.double() - b).abs().max() / b.abs().max())
+        errs["gdp_dx"] = float((gd[0].double() - gd_ref[0][r0:r1]).abs().max())
+        for name, a, b in zip(("dwp", "dbp", "dwg", "dbg"), gd[1:], gd_ref[1:]):
+            errs[name] = float((a.double() - b).abs().max() / b.abs().max())
+        queue.put((rank, "ok", errs))
+        dist.destroy_process_group()
+    except Exception as e:
+        queue.put((rank, "error", "%s: %s\n%s" % (type(e).__name__, e, traceback.format_exc())))
+
+
+def test_sharded_ln_gdp_matches_single_process():
+    """Row shards of 11 rows over 2 ranks: dx row-local, parameter gradients (reduced in f32 via
+    one all-reduce of a flat buffer) equal the full-batch oracle's to f32 rounding."""
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ln_gdp_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict((r, (s, e)) for r, s, e in (queue.get(timeout=120) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    for rank in (0, 1):
+        status, errs = results[rank]
+        assert status == "ok", errs
+        for name, err in errs.items():
+            assert err < (1e-12 if name.endswith("dx") else 1e-6), (rank, name, err)

@@ -1,0 +1,108 @@
+"""Row sharding on two GPUs with NCCL (skipped with fewer than two GPUs).
+
+Attention (ShardedAttention: dbias all-reduced on a side stream) and LayerNorm / GDP
+(ShardedLnGdp: one all-reduce of the flat parameter-gradient buffer), each rank on its own GPU,
+against the same kernels run on the full batch on one GPU.  Row-local outputs computed
+without reductions across CTAs match exactly (a row's result does not depend on the other
+rows); dq/dv to their last bit, and the reduced gradients to f32 summation-order rounding.  NVLS is off (NCCL_NVLS_ENABLE=0) as for every multi-rank test here.
+"""
+
+import os
+import socket
+import sys
+import traceback
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, queue):
+    try:
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        sys.path[:0] = [REPO, os.path.join(REPO, "colabfold-legacy-kernels_b200", "src")]
+        import torch.distributed as dist
+        import oracle
+        from colabfold_legacy_kernels import torch_ops
+        from colabfold_legacy_kernels.parallel import ShardedAttention, ShardedLnGdp
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", init_method="tcp://127.0.0.1:%d" % port, rank=rank,
+                                world_size=world, timeout=timedelta(seconds=60))
+        errs = {}
+        # attention, config C3's shape class at 24 rows x 256
+        cfg = oracle.configs.scaled(oracle.configs.C3, n=24, s=256)
+        inp = oracle.configs.make_attention_inputs(cfg, device="cpu")
+        t = {k: (v.to(dev) if torch.is_tensor(v) else v) for k, v in inp.items()}
+        sa = ShardedAttention()
+        r0, r1 = sa.rows(t["q"].shape[0])
+        res = sa.step(*(t[x][r0:r1] for x in ("q", "k", "v")), t["bias"], t["kmask"][r0:r1],
+                      t["dout"][r0:r1], t["scale"])
+        out, lse = torch_ops.attention_fwd(t["q"], t["k"], t["v"], t["bias"], t["kmask"],
+                                           t["scale"])
+        dq, dk, dv, db = torch_ops.attention_bwd(t["q"], t["k"], t["v"], t["bias"], t["kmask"],
+                                                 out, lse, t["dout"], t["scale"])
+        torch.cuda.synchronize()
+        errs["attn_out"] = float((res.out.float() - out[r0:r1].float()).abs().max())
+        # dq, dv: sums of partials reduced in f32 in a timing-dependent order, then rounded to
+        # 16 bits, so they may differ in the last bit
+        errs["attn_dq_bf"] = float((res.dq.float() - dq[r0:r1].float()).abs().max()
+                                   / dq.float().abs().max())
+        errs["attn_dv_bf"] = float((res.dv.float() - dv[r0:r1].float()).abs().max()
+                                   / dv.float().abs().max())
+        errs["attn_dbias_rel"] = float((res.dbias - db).abs().max() / db.abs().max())
+        # LayerNorm + GDP, config C4's shape class at 3000 rows
+        ci = oracle.configs.make_ln_gdp_inputs(oracle.configs.LnGdpConfig("c4_small", 3000, 128,
+                                                                          256, 3), device=dev)
+        sh = ShardedLnGdp()
+        m0, m1 = sh.rows(3000)
+        x, g, dy = ci["x"], ci["gamma"], ci["dy"]
+        ln = sh.layer_norm_bwd(x[m0:m1], g, dy[m0:m1], 1e-5)
+        gd = sh.gdp_bwd(x[m0:m1], ci["wp"], ci["bp"], ci["wg"], ci["bg"], ci["mask"][m0:m1],
+                        ci["dout"][m0:m1])
+        ln_ref = torch_ops.layer_norm_bwd(x, g, dy, 1e-5)
+        gd_ref = torch_ops.gdp_bwd(x, ci["wp"], ci["bp"], ci["wg"], ci["bg"], ci["mask"],
+                                   ci["dout"])
+        torch.cuda.synchronize()
+        errs["ln_dx"] = float((ln[0].float() - ln_ref[0][m0:m1].float()).abs().max())
+        errs["gdp_dx"] = float((gd[0].float() - gd_ref[0][m0:m1].float()).abs().max())
+        for name, a, b in (("dgamma_rel", ln[1], ln_ref[1]), ("dbeta_rel", ln[2], ln_ref[2]),
+                           ("dwp_rel", gd[1], gd_ref[1]), ("dbp_rel", gd[2], gd_ref[2]),
+                           ("dwg_rel", gd[3], gd_ref[3]), ("dbg_rel", gd[4], gd_ref[4])):
+            errs[name] = float((a - b).abs().max() / b.abs().max())
+        queue.put((rank, "ok", errs))
+        dist.destroy_process_group()
+    except Exception as e:
+        queue.put((rank, "error", "%s: %s\n%s" % (type(e).__name__, e, traceback.format_exc())))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_sharding_matches_one_gpu():
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict((r, (s, e)) for r, s, e in (queue.get(timeout=300) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    for rank in (0, 1):
+        status, errs = results[rank]
+        assert status == "ok", errs
+        for name, err in errs.items():
+            bound = 1e-5 if name.endswith("_rel") else (1e-2 if name.endswith("_bf") else 0.0)
+            assert err <= bound, (rank, name, err)
