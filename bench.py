@@ -334,13 +334,50 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
         wall = time.perf_counter() - wall0
+        graph_ms = []
+        if not args.no_graph:
+            # The same step captured once in a CUDA graph (the dbias all-reduce included) and
+            # replayed: the host's per-launch work leaves the timed region, which matters when
+            # a step is short (many GPUs).  W warm-up replays, then K timed ones, L2 flushed
+            # between them as above.
+            graph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                step()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph):
+                step()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            for _ in range(args.warmup):
+                graph.replay()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            for _ in range(args.steps):
+                flush.zero_()  # untimed: evicts L2 between steps
+                g0.record()
+                graph.replay()
+                g1.record()
+                torch.cuda.synchronize()
+                graph_ms.append(g0.elapsed_time(g1))
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            del graph  # holds NCCL work: released before the process group goes away
     ms = sum(step_ms) / len(step_ms)
     ms_fwd = sum(fwd_ms) / len(fwd_ms)
     ms_bwd = sum(bwd_ms) / len(bwd_ms)
+    ms_graph = sum(graph_ms) / len(graph_ms) if graph_ms else 0.0
     if world > 1:
-        t = torch.tensor([ms, ms_fwd, ms_bwd], device=dev)
+        t = torch.tensor([ms, ms_fwd, ms_bwd, ms_graph], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ms_fwd, ms_bwd = t.tolist()
+        ms, ms_fwd, ms_bwd, ms_graph = t.tolist()
+    ms_eager = ms
+    if graph_ms:
+        ms = ms_graph
     total_flops = attn_flops(N_RES, HEADS, N_RES, HEAD_DIM)
     value = total_flops / (ms * 1e-3) / 1e12
 
@@ -435,7 +472,10 @@ def run_ours(args, rank, world, local_rank):
         "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "tri_start_768 fwd+bwd (C3)", "n_res": N_RES, "heads": HEADS,
                    "head_dim": HEAD_DIM, "rows_per_gpu": n, "parallelism": "rows%d" % world,
-                   "l2": "flushed between steps (256 MB write, outside the timed events)"},
+                   "l2": "flushed between steps (256 MB write, outside the timed events)",
+                   "launch": ("one CUDA graph replay per step (the step captured once, the dbias "
+                              "all-reduce included)" if ms_graph else "eager launches"),
+                   "eager_ms_per_step": ms_eager},
         "gpu_launches": 6 * args.steps,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": me2e, "steps": args.e2e_steps,
@@ -636,6 +676,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=32,
                     help="attention rows in one CPU sample (reference arm and cpu_baseline)")
     ap.add_argument("--skip-extras", action="store_true", help="skip LayerNorm/GDP lines")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time the eager step only (no CUDA-graph replay)")
     ap.add_argument("--skip-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--rows", type=int, default=0,
                     help="profiling only: attention rows on this GPU instead of 768/N")
