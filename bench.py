@@ -476,7 +476,7 @@ def run_ours(args, rank, world, local_rank):
                    "launch": ("one CUDA graph replay per step (the step captured once, the dbias "
                               "all-reduce included)" if ms_graph else "eager launches"),
                    "eager_ms_per_step": ms_eager},
-        "gpu_launches": 6 * args.steps,
+        "gpu_launches": 4 * args.steps,  # attn_fwd, rowstat, attn_bwd, f32_to_16 per step
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": me2e, "steps": args.e2e_steps,
                 "overlap": "double-buffered: host->device copies of step i+1 and device->host "

@@ -644,16 +644,35 @@ __global__ void attn_bwd_rowstat_kernel(const T* __restrict__ out, const T* __re
     dst[128] = nd;
 }
 
-// dst[i] = (16-bit) src[i], 8 elements per thread.
+// dst_s[i] = (16-bit) src_s[i] for the three accumulators s = dq, dk, dv in one launch, 8
+// elements per thread and step (n8[s] groups of 8 each).
+struct ConvertJob {
+    const float* src[3];
+    void* dst[3];
+    int64_t n8[3];
+};
+
 template <typename T>
-__global__ void f32_to_16_kernel(const float* __restrict__ src, T* __restrict__ dst, int64_t n8) {
+__global__ void f32_to_16_kernel(const ConvertJob job) {
     using E = Elem<T>;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+    const int64_t total = job.n8[0] + job.n8[1] + job.n8[2];
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const float4 a = *reinterpret_cast<const float4*>(src + i * 8);
-        const float4 b = *reinterpret_cast<const float4*>(src + i * 8 + 4);
-        st_global_v4(dst + i * 8, make_uint4(E::pack(a.x, a.y), E::pack(a.z, a.w),
-                                             E::pack(b.x, b.y), E::pack(b.z, b.w)));
+        int s = 0;
+        int64_t k = i;
+        if (k >= job.n8[0]) {
+            k -= job.n8[0];
+            s = 1;
+            if (k >= job.n8[1]) {
+                k -= job.n8[1];
+                s = 2;
+            }
+        }
+        const float4 a = *reinterpret_cast<const float4*>(job.src[s] + k * 8);
+        const float4 b = *reinterpret_cast<const float4*>(job.src[s] + k * 8 + 4);
+        st_global_v4(static_cast<T*>(job.dst[s]) + k * 8,
+                     make_uint4(E::pack(a.x, a.y), E::pack(a.z, a.w), E::pack(b.x, b.y),
+                                E::pack(b.z, b.w)));
     }
 }
 
@@ -753,11 +772,9 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
     if (!(phases & 4)) {
         return CFK_OK;
     }
-    const int cgrid = dev.num_sms * 8;
-    f32_to_16_kernel<T><<<cgrid, 256, 0, st>>>(dq_acc, static_cast<T*>(dq), rows * D / 8);
     const int64_t kv8 = static_cast<int64_t>(N) * H * Sk * D / 8;
-    f32_to_16_kernel<T><<<cgrid, 256, 0, st>>>(dk_acc, static_cast<T*>(dk), kv8);
-    f32_to_16_kernel<T><<<cgrid, 256, 0, st>>>(dv_acc, static_cast<T*>(dv), kv8);
+    const ConvertJob job{{dq_acc, dk_acc, dv_acc}, {dq, dk, dv}, {rows * D / 8, kv8, kv8}};
+    f32_to_16_kernel<T><<<dev.num_sms * 8, 256, 0, st>>>(job);
     return check_launch("attn_bwd convert");
 }
 
