@@ -78,3 +78,24 @@ def test_bad_arguments_rejected_without_device(libpath):
 def test_workspace_queries_need_no_device(libpath):
     from colabfold_legacy_kernels import cabi
     assert cabi.workspace_size("cfk_ln_bwd_workspace_size", 1 << 20, 128) > 0
+
+
+def test_ln_gdp_fwd_arguments_without_device(libpath):
+    """cfk_ln_gdp_fwd: the tcgen05 shapes need no workspace, others stage LayerNorm(z) there;
+    bad dtype / eps / null buffers are rejected before any device call."""
+    from colabfold_legacy_kernels import cabi
+    assert cabi.workspace_size("cfk_ln_gdp_fwd_workspace_size", 1 << 20, 128, 256) == 0
+    assert cabi.workspace_size("cfk_ln_gdp_fwd_workspace_size", 1000, 40, 24) == 1000 * 40 * 2
+    args = [None] * 12  # z .. rstd, workspace pointers
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_ln_gdp_fwd", None, 9, None, None, None, 1e-5, *args[:8], None, 0,
+                  16, 128, 256)
+    assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT and "dtype" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_ln_gdp_fwd", None, cabi.CFK_BF16, None, None, None, -1.0, *args[:8], None,
+                  0, 16, 128, 256)
+    assert "eps" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_ln_gdp_fwd", None, cabi.CFK_BF16, None, None, None, 1e-5, *args[:8], None,
+                  0, 16, 128, 256)
+    assert "null buffer" in e.value.message
