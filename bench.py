@@ -486,11 +486,67 @@ def run_ours(args, rank, world, local_rank):
         "wall_s_timed": wall,
     }
     if world == 1 and not args.skip_extras:
+        result["attention_views"] = bench_attention_views(dev, ms_eager)
         result["layernorm"] = bench_layernorm(dev, pk)
         result["gdp"] = bench_gdp(dev, pk)
     elif not args.skip_extras:
         result.update(bench_ln_gdp_sharded(dev, pk, world))
     return result
+
+
+def bench_attention_views(dev, packed_ms, steps=10):
+    """The C3 step (fwd + the three backward launches) with q, k, v, dout, out, dq, dk, dv as
+    [N,H,S,D] views of [S,N,H,D] storage: the layout of triangle attention around the ending
+    node (attention over the first residue axis), passed to the kernels as strides
+    (cfk_attn_*_strided) instead of transposed copies.  Eager launches, L2 flushed between
+    steps; compared with the packed eager step of the same run."""
+    import torch
+    import oracle
+    from colabfold_legacy_kernels import torch_ops
+
+    full = oracle.configs.make_attention_inputs(oracle.configs.C3, device=dev)
+
+    def as_view(t):  # same values, stored [S, N, H, D], viewed [N, H, S, D]
+        return t.permute(2, 0, 1, 3).contiguous().permute(1, 2, 0, 3)
+
+    def empty_view(t):
+        return torch.empty_like(t.permute(2, 0, 1, 3)).permute(1, 2, 0, 3)
+
+    q, k, v, dout = (as_view(full[x]) for x in ("q", "k", "v", "dout"))
+    bias, kmask, scale = full["bias"], full["kmask"], full["scale"]
+    del full
+    n = q.shape[0]
+    out = empty_view(q)
+    lse = torch.empty((n, HEADS, N_RES), dtype=torch.float32, device=dev)
+    grads = (empty_view(q), empty_view(k), empty_view(v),
+             torch.empty((HEADS, N_RES, N_RES), dtype=torch.float32, device=dev))
+    ws = torch_ops.attention_bwd_workspace(n, HEADS, N_RES, N_RES, HEAD_DIM, dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        torch_ops.attention_fwd(q, k, v, bias, kmask, scale, out=out, lse=lse)
+        for ph in range(3):
+            torch_ops.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=ws,
+                                    grads=grads, phase=ph)
+
+    for _ in range(3):
+        step()
+    ts = []
+    for _ in range(steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    ms = sorted(ts)[len(ts) // 2]
+    return {"workload": "tri_end_768 fwd+bwd: [S,N,H,D] storage viewed as [N,H,S,D]",
+            "metric": METRIC, "unit": UNIT,
+            "value": round(attn_flops(n, HEADS, N_RES, HEAD_DIM) / (ms * 1e-3) / 1e12, 1),
+            "ms_per_step": round(ms, 4), "packed_eager_ms_per_step": round(packed_ms, 4),
+            "launch": "eager", "steps": steps,
+            "l2": "flushed between steps (256 MB write, outside the timed events)"}
 
 
 def bench_ln_gdp_sharded(dev, pk, world, steps=20):

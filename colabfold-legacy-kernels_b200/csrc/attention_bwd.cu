@@ -223,10 +223,10 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
                     const int bh = b * p.H + h;
                     if (elect_one()) {
                         mbar_arrive_expect_tx(&kv_full[s], 4 * G::kTileBytes + 1024);
-                        tma_load_3d(stage + C::kOffSK, &tm_k, &kv_full[s], 0, j0, bh);
-                        tma_load_3d(stage + C::kOffSQ, &tm_q, &kv_full[s], 0, i0, bh);
-                        tma_load_3d(stage + C::kOffSV, &tm_v, &kv_full[s], 0, j0, bh);
-                        tma_load_3d(stage + C::kOffSdO, &tm_do, &kv_full[s], 0, i0, bh);
+                        tma_load_4d(stage + C::kOffSK, &tm_k, &kv_full[s], 0, j0, h, b);
+                        tma_load_4d(stage + C::kOffSQ, &tm_q, &kv_full[s], 0, i0, h, b);
+                        tma_load_4d(stage + C::kOffSV, &tm_v, &kv_full[s], 0, j0, h, b);
+                        tma_load_4d(stage + C::kOffSdO, &tm_do, &kv_full[s], 0, i0, h, b);
                         bulk_load(stage + C::kOffRS,
                                   p.rowstat + (static_cast<int64_t>(bh) * p.n_it + itile) * 256,
                                   1024, &kv_full[s]);
@@ -608,7 +608,8 @@ done:
 template <typename T, int D>
 __global__ void attn_bwd_rowstat_kernel(const T* __restrict__ out, const T* __restrict__ dout,
                                         const float* __restrict__ lse, float* __restrict__ rowstat,
-                                        int64_t bh_count, int Sq, int n_it, float scale) {
+                                        int64_t bh_count, int Sq, int n_it, float scale,
+                                        const RowStrides out_view, const RowStrides dout_view) {
     using E = Elem<T>;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (r >= bh_count * n_it * 128) {
@@ -621,11 +622,13 @@ __global__ void attn_bwd_rowstat_kernel(const T* __restrict__ out, const T* __re
     float nl = 0.f, nd = 0.f;
     if (i < Sq) {
         const int64_t row = bh * Sq + i;
+        const T* orow = out + view_row_offset(out_view, row, D);
+        const T* drow = dout + view_row_offset(dout_view, row, D);
         float acc = 0.f;
 #pragma unroll
         for (int c = 0; c < D / 8; ++c) {
-            const uint4 a = ld_global_nc_v4(out + row * D + c * 8);
-            const uint4 b = ld_global_nc_v4(dout + row * D + c * 8);
+            const uint4 a = ld_global_nc_v4(orow + c * 8);
+            const uint4 b = ld_global_nc_v4(drow + c * 8);
             const uint32_t wa[4] = {a.x, a.y, a.z, a.w};
             const uint32_t wb[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -642,38 +645,6 @@ __global__ void attn_bwd_rowstat_kernel(const T* __restrict__ out, const T* __re
     float* dst = rowstat + (bh * n_it + it) * 256 + ii;
     dst[0] = nl;
     dst[128] = nd;
-}
-
-// dst_s[i] = (16-bit) src_s[i] for the three accumulators s = dq, dk, dv in one launch, 8
-// elements per thread and step (n8[s] groups of 8 each).
-struct ConvertJob {
-    const float* src[3];
-    void* dst[3];
-    int64_t n8[3];
-};
-
-template <typename T>
-__global__ void f32_to_16_kernel(const ConvertJob job) {
-    using E = Elem<T>;
-    const int64_t total = job.n8[0] + job.n8[1] + job.n8[2];
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        int s = 0;
-        int64_t k = i;
-        if (k >= job.n8[0]) {
-            k -= job.n8[0];
-            s = 1;
-            if (k >= job.n8[1]) {
-                k -= job.n8[1];
-                s = 2;
-            }
-        }
-        const float4 a = *reinterpret_cast<const float4*>(job.src[s] + k * 8);
-        const float4 b = *reinterpret_cast<const float4*>(job.src[s] + k * 8 + 4);
-        st_global_v4(static_cast<T*>(job.dst[s]) + k * 8,
-                     make_uint4(E::pack(a.x, a.y), E::pack(a.z, a.w), E::pack(b.x, b.y),
-                                E::pack(b.z, b.w)));
-    }
 }
 
 constexpr size_t align256(size_t x) {
@@ -701,7 +672,8 @@ template <typename T, int D>
 int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                const void* v, const void* bias, const uint8_t* kmask, const void* out,
                const float* lse, const void* dout, void* dq, void* dk, void* dv, float* dbias,
-               uint8_t* ws, int N, int H, int Sq, int Sk, float scale, int phases) {
+               uint8_t* ws, int N, int H, int Sq, int Sk, float scale, int phases,
+               const RowView* views) {
     using C = BwdCfg<D>;
     using G = Geo<D>;
     const BwdWorkspace wl = bwd_workspace(N, H, Sq, Sk, D);
@@ -711,13 +683,11 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
     float* rowstat = reinterpret_cast<float*>(ws + wl.rs_off);
 
     const uint64_t nh = static_cast<uint64_t>(N) * H;
-    const uint64_t row = 2ull * D;
     CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
-    CFK_TRY(make_tmap_3d(&tq, q, D, Sq, nh, row, row * Sq, D, kBM, 1, G::kSwizzleBytes, "bwd q"));
-    CFK_TRY(make_tmap_3d(&tdo, dout, D, Sq, nh, row, row * Sq, D, kBM, 1, G::kSwizzleBytes,
-                         "bwd dout"));
-    CFK_TRY(make_tmap_3d(&tk, k, D, Sk, nh, row, row * Sk, D, kBN, 1, G::kSwizzleBytes, "bwd k"));
-    CFK_TRY(make_tmap_3d(&tv, v, D, Sk, nh, row, row * Sk, D, kBN, 1, G::kSwizzleBytes, "bwd v"));
+    CFK_TRY(make_tmap_rows(&tq, q, views[0], D, kBM, G::kSwizzleBytes, "bwd q"));
+    CFK_TRY(make_tmap_rows(&tk, k, views[1], D, kBN, G::kSwizzleBytes, "bwd k"));
+    CFK_TRY(make_tmap_rows(&tv, v, views[2], D, kBN, G::kSwizzleBytes, "bwd v"));
+    CFK_TRY(make_tmap_rows(&tdo, dout, views[4], D, kBM, G::kSwizzleBytes, "bwd dout"));
     const uint64_t frow = 4ull * D;
     CFK_TRY(make_tmap_3d(&tdq, dq_acc, D, Sq, nh, frow, frow * Sq, C::kPW, kBM, 1, C::kRowB,
                          "bwd dq acc", true));
@@ -758,7 +728,8 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
         const int64_t prow = static_cast<int64_t>(nh) * p.n_it * 128;
         attn_bwd_rowstat_kernel<T, D><<<static_cast<int>((prow + 255) / 256), 256, 0, st>>>(
             static_cast<const T*>(out), static_cast<const T*>(dout), lse, rowstat,
-            static_cast<int64_t>(nh), Sq, p.n_it, scale);
+            static_cast<int64_t>(nh), Sq, p.n_it, scale, row_strides(views[3], D),
+            row_strides(views[4], D));
         CFK_TRY(check_launch("attn_bwd_rowstat"));
     }
     if (phases & 2) {
@@ -773,7 +744,12 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
         return CFK_OK;
     }
     const int64_t kv8 = static_cast<int64_t>(N) * H * Sk * D / 8;
-    const ConvertJob job{{dq_acc, dk_acc, dv_acc}, {dq, dk, dv}, {rows * D / 8, kv8, kv8}};
+    const ConvertJob job{{dq_acc, dk_acc, dv_acc},
+                         {dq, dk, dv},
+                         {rows * D / 8, kv8, kv8},
+                         {row_strides(views[5], D), row_strides(views[6], D),
+                          row_strides(views[7], D)},
+                         d8_log2(D)};
     f32_to_16_kernel<T><<<dev.num_sms * 8, 256, 0, st>>>(job);
     return check_launch("attn_bwd convert");
 }
@@ -782,11 +758,12 @@ template <typename T>
 int dispatch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                  const void* v, const void* bias, const uint8_t* kmask, const void* out,
                  const float* lse, const void* dout, void* dq, void* dk, void* dv, float* dbias,
-                 uint8_t* ws, int N, int H, int Sq, int Sk, int D, float scale, int phases) {
+                 uint8_t* ws, int N, int H, int Sq, int Sk, int D, float scale, int phases,
+                 const RowView* views) {
 #define CFK_BWD_D(DD)                                                                              \
     if (D == DD) {                                                                                 \
         return launch_bwd<T, DD>(st, dev, q, k, v, bias, kmask, out, lse, dout, dq, dk, dv, dbias, \
-                                 ws, N, H, Sq, Sk, scale, phases);                                 \
+                                 ws, N, H, Sq, Sk, scale, phases, views);                          \
     }
     CFK_BWD_D(8)
     CFK_BWD_D(16)
@@ -815,37 +792,52 @@ extern "C" int cfk_attn_bwd_workspace_size(int64_t N, int64_t H, int64_t Sq, int
 
 namespace {
 
-// Shared body of cfk_attn_bwd (phases = 7) and cfk_attn_bwd_phase (one bit).
+// Shared body of cfk_attn_bwd (phases = 7), cfk_attn_bwd_phase (one bit) and their strided
+// forms (user_views: q, k, v, out, dout, dq, dk, dv; NULL = packed).
 int attn_bwd_entry(const char* fn, int phases, cfk_stream_t stream, cfk_dtype dtype,
                    const void* q, const void* k, const void* v, const void* bias,
                    const uint8_t* kmask, const void* out, const float* lse, const void* dout,
                    void* dq, void* dk, void* dv, float* dbias, void* workspace,
                    size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
-                   float scale) {
+                   float scale, const cfk_view* user_views) {
     clear_error();
     CFK_TRY(check_attn_args(fn, dtype, N, H, Sq, Sk, D));
+    static const char* const names[8] = {"q", "k", "v", "out", "dout", "dq", "dk", "dv"};
+    RowView views[8];
+    for (int t = 0; t < 8; ++t) {
+        const int64_t S = (t == 1 || t == 2 || t == 6 || t == 7) ? Sk : Sq;
+        CFK_TRY(view_of(fn, names[t], user_views ? &user_views[t] : nullptr, N, H, S, D,
+                        &views[t]));
+    }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (H == 0 || Sq == 0 || Sk == 0 || N == 0) {
         // Empty: gradients are zero (dq for Sk == 0; dk, dv for Sq == 0; dbias always).
         if (!(phases & 4)) {
             return CFK_OK;
         }
-        cudaError_t e = cudaSuccess;
-        if (dbias && H * Sq * Sk > 0) {
-            e = cudaMemsetAsync(dbias, 0, static_cast<size_t>(H * Sq * Sk) * 4, st);
+        if (dbias && H * Sq * Sk > 0 &&
+            cudaMemsetAsync(dbias, 0, static_cast<size_t>(H * Sq * Sk) * 4, st) != cudaSuccess) {
+            return fail(CFK_ERR_LAUNCH, "%s: memset failed", fn);
         }
-        if (e == cudaSuccess && dq && N * H * Sq * D > 0) {
-            e = cudaMemsetAsync(dq, 0, static_cast<size_t>(N * H * Sq * D) * 2, st);
+        const int64_t nq8 = dq ? N * H * Sq * D / 8 : 0;
+        const int64_t nk8 = dk ? N * H * Sk * D / 8 : 0;
+        const int64_t nv8 = dv ? N * H * Sk * D / 8 : 0;
+        if (nq8 + nk8 + nv8 == 0) {
+            return CFK_OK;
         }
-        if (e == cudaSuccess && N * H * Sk * D > 0) {
-            if (dk) {
-                e = cudaMemsetAsync(dk, 0, static_cast<size_t>(N * H * Sk * D) * 2, st);
-            }
-            if (e == cudaSuccess && dv) {
-                e = cudaMemsetAsync(dv, 0, static_cast<size_t>(N * H * Sk * D) * 2, st);
-            }
+        if (!aligned16(dq) || !aligned16(dk) || !aligned16(dv)) {
+            return fail(CFK_ERR_INVALID_ARGUMENT, "%s: dq, dk and dv must be 16-byte aligned", fn);
         }
-        return e == cudaSuccess ? CFK_OK : fail(CFK_ERR_LAUNCH, "%s: memset failed", fn);
+        DeviceInfo dev;
+        CFK_TRY(current_device(&dev));
+        const attn::ConvertJob job{{nullptr, nullptr, nullptr},
+                                   {dq, dk, dv},
+                                   {nq8, nk8, nv8},
+                                   {attn::row_strides(views[5], D), attn::row_strides(views[6], D),
+                                    attn::row_strides(views[7], D)},
+                                   attn::d8_log2(static_cast<int>(D))};
+        attn::f32_to_16_kernel<__half><<<dev.num_sms * 8, 256, 0, st>>>(job);
+        return check_launch("attn_bwd zero");
     }
     if (!q || !k || !v || !bias || !kmask || !out || !lse || !dout || !dq || !dk || !dv ||
         !dbias) {
@@ -870,9 +862,9 @@ int attn_bwd_entry(const char* fn, int phases, cfk_stream_t stream, cfk_dtype dt
     return dtype == CFK_BF16
                ? attn::dispatch_bwd<__nv_bfloat16>(st, dev, q, k, v, bias, kmask, out, lse, dout,
                                                    dq, dk, dv, dbias, ws, n, h, sq, sk, d, scale,
-                                                   phases)
+                                                   phases, views)
                : attn::dispatch_bwd<__half>(st, dev, q, k, v, bias, kmask, out, lse, dout, dq, dk,
-                                            dv, dbias, ws, n, h, sq, sk, d, scale, phases);
+                                            dv, dbias, ws, n, h, sq, sk, d, scale, phases, views);
 }
 
 } // namespace
@@ -884,8 +876,39 @@ extern "C" int cfk_attn_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* q,
                             size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq, int64_t Sk,
                             int64_t D, float scale) {
     return attn_bwd_entry("cfk_attn_bwd", 7, stream, dtype, q, k, v, bias, kmask, out, lse, dout,
-                          dq, dk, dv, dbias, workspace, workspace_bytes, N, H, Sq, Sk, D, scale);
+                          dq, dk, dv, dbias, workspace, workspace_bytes, N, H, Sq, Sk, D, scale,
+                          nullptr);
 }
+
+extern "C" int cfk_attn_bwd_strided(cfk_stream_t stream, cfk_dtype dtype, const void* q,
+                                    const void* k, const void* v, const void* bias,
+                                    const uint8_t* kmask, const void* out, const float* lse,
+                                    const void* dout, void* dq, void* dk, void* dv, float* dbias,
+                                    void* workspace, size_t workspace_bytes, int64_t N, int64_t H,
+                                    int64_t Sq, int64_t Sk, int64_t D, float scale,
+                                    const cfk_view* views) {
+    return attn_bwd_entry("cfk_attn_bwd_strided", 7, stream, dtype, q, k, v, bias, kmask, out,
+                          lse, dout, dq, dk, dv, dbias, workspace, workspace_bytes, N, H, Sq, Sk,
+                          D, scale, views);
+}
+
+namespace {
+
+int bwd_phase(const char* fn, int phase, cfk_stream_t stream, cfk_dtype dtype, const void* q,
+              const void* k, const void* v, const void* bias, const uint8_t* kmask,
+              const void* out, const float* lse, const void* dout, void* dq, void* dk, void* dv,
+              float* dbias, void* workspace, size_t workspace_bytes, int64_t N, int64_t H,
+              int64_t Sq, int64_t Sk, int64_t D, float scale, const cfk_view* views) {
+    if (phase < 0 || phase > 2) {
+        clear_error();
+        return fail(CFK_ERR_INVALID_ARGUMENT, "%s: phase %d not in {0,1,2}", fn, phase);
+    }
+    return attn_bwd_entry(fn, 1 << phase, stream, dtype, q, k, v, bias, kmask, out, lse, dout,
+                          dq, dk, dv, dbias, workspace, workspace_bytes, N, H, Sq, Sk, D, scale,
+                          views);
+}
+
+} // namespace
 
 extern "C" int cfk_attn_bwd_phase(int phase, cfk_stream_t stream, cfk_dtype dtype,
                                   const void* q, const void* k, const void* v, const void* bias,
@@ -893,13 +916,20 @@ extern "C" int cfk_attn_bwd_phase(int phase, cfk_stream_t stream, cfk_dtype dtyp
                                   const void* dout, void* dq, void* dk, void* dv, float* dbias,
                                   void* workspace, size_t workspace_bytes, int64_t N, int64_t H,
                                   int64_t Sq, int64_t Sk, int64_t D, float scale) {
-    if (phase < 0 || phase > 2) {
-        clear_error();
-        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_attn_bwd_phase: phase %d not in {0,1,2}",
-                    phase);
-    }
-    return attn_bwd_entry("cfk_attn_bwd_phase", 1 << phase, stream, dtype, q, k, v, bias, kmask,
-                          out, lse, dout, dq, dk, dv, dbias, workspace, workspace_bytes, N, H, Sq,
-                          Sk, D, scale);
+    return bwd_phase("cfk_attn_bwd_phase", phase, stream, dtype, q, k, v, bias, kmask, out, lse,
+                     dout, dq, dk, dv, dbias, workspace, workspace_bytes, N, H, Sq, Sk, D, scale,
+                     nullptr);
 }
 
+extern "C" int cfk_attn_bwd_phase_strided(int phase, cfk_stream_t stream, cfk_dtype dtype,
+                                          const void* q, const void* k, const void* v,
+                                          const void* bias, const uint8_t* kmask,
+                                          const void* out, const float* lse, const void* dout,
+                                          void* dq, void* dk, void* dv, float* dbias,
+                                          void* workspace, size_t workspace_bytes, int64_t N,
+                                          int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                          float scale, const cfk_view* views) {
+    return bwd_phase("cfk_attn_bwd_phase_strided", phase, stream, dtype, q, k, v, bias, kmask,
+                     out, lse, dout, dq, dk, dv, dbias, workspace, workspace_bytes, N, H, Sq, Sk,
+                     D, scale, views);
+}

@@ -10,6 +10,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "host.h"
 #include "sm100.cuh"
 
 namespace cfk {
@@ -107,6 +108,96 @@ inline uint16_t mask_bias_bits(float scale) {
     }
     return static_cast<uint16_t>(0x8000u | (static_cast<uint32_t>(e + 127) << 7));
 }
+
+// A [N, H, S, D] tensor as the kernels address it: element strides of the batch, head and
+// sequence axes (D contiguous) and the extents H, S needed to split a row number.
+struct RowStrides {
+    int64_t b, h, s;
+    int H, S;
+    int packed; // b = H S D, h = S D, s = D: row r starts at r D
+};
+
+// Element offset of row r = (n H + h) S + i of the view.
+__device__ __forceinline__ int64_t view_row_offset(const RowStrides& v, int64_t r, int d) {
+    if (v.packed) {
+        return r * d;
+    }
+    int64_t bh, n;
+    int i, h;
+    if (r < (1ll << 32)) {
+        // 32-bit division is much cheaper than 64-bit
+        const uint32_t r32 = static_cast<uint32_t>(r);
+        const uint32_t bh32 = r32 / static_cast<uint32_t>(v.S);
+        i = static_cast<int>(r32 - bh32 * static_cast<uint32_t>(v.S));
+        const uint32_t n32 = bh32 / static_cast<uint32_t>(v.H);
+        h = static_cast<int>(bh32 - n32 * static_cast<uint32_t>(v.H));
+        bh = bh32;
+        n = n32;
+    } else {
+        bh = r / v.S;
+        i = static_cast<int>(r - bh * v.S);
+        n = bh / v.H;
+        h = static_cast<int>(bh - n * v.H);
+    }
+    return n * v.b + h * v.h + static_cast<int64_t>(i) * v.s;
+}
+
+namespace {
+
+// RowStrides of a host-side RowView (host.h) of a tensor with head dim d.
+inline RowStrides row_strides(const RowView& v, int64_t d) {
+    return RowStrides{v.b, v.h, v.s, static_cast<int>(v.H), static_cast<int>(v.S),
+                      is_packed(v, d) ? 1 : 0};
+}
+
+// log2(d / 8) for d in {8, 16, 32, 64}
+inline int d8_log2(int d) {
+    return d == 8 ? 0 : d == 16 ? 1 : d == 32 ? 2 : 3;
+}
+
+// dst_t = (16-bit) src_t for up to three tensors t in one launch, or zeros where src_t is NULL:
+// src_t packed f32 [N, H, S_t, D] (n8[t] groups of 8 elements), dst_t written through its view.
+// 8 elements per thread and step; D = 8 << d8_log2.
+struct ConvertJob {
+    const float* src[3];
+    void* dst[3];
+    int64_t n8[3];
+    RowStrides view[3];
+    int d8_log2;
+};
+
+template <typename T>
+__global__ void f32_to_16_kernel(const ConvertJob job) {
+    using E = Elem<T>;
+    const int64_t total = job.n8[0] + job.n8[1] + job.n8[2];
+    const int d = 8 << job.d8_log2;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int t = 0;
+        int64_t k = i;
+        if (k >= job.n8[0]) {
+            k -= job.n8[0];
+            t = 1;
+            if (k >= job.n8[1]) {
+                k -= job.n8[1];
+                t = 2;
+            }
+        }
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (job.src[t]) {
+            const float4 a = *reinterpret_cast<const float4*>(job.src[t] + k * 8);
+            const float4 b = *reinterpret_cast<const float4*>(job.src[t] + k * 8 + 4);
+            val = make_uint4(E::pack(a.x, a.y), E::pack(a.z, a.w), E::pack(b.x, b.y),
+                             E::pack(b.z, b.w));
+        }
+        const int64_t r = k >> job.d8_log2;
+        const int c = static_cast<int>(k & ((1 << job.d8_log2) - 1));
+        st_global_v4(static_cast<T*>(job.dst[t]) + view_row_offset(job.view[t], r, d) + c * 8,
+                     val);
+    }
+}
+
+} // namespace
 
 } // namespace attn
 } // namespace cfk

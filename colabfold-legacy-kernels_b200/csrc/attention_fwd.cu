@@ -87,6 +87,7 @@ struct FwdParams {
     const uint8_t* kmask;
     const uint16_t* bias; // raw pointer (used when the bias tile is not loaded by TMA)
     uint16_t* out;
+    int64_t ob, oh, os; // element strides of out's batch, head and query axes
     float* lse;
     int N, H, Sq, Sk;
     int n_qt, n_kt, n_groups;
@@ -215,8 +216,8 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                 }
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&bars[C::kBarQFull + w], G::kTileBytes);
-                    tma_load_3d(smem + C::kOffQ + w * C::kTile, &tm_q, &bars[C::kBarQFull + w], 0,
-                                q0, b * p.H + h);
+                    tma_load_4d(smem + C::kOffQ + w * C::kTile, &tm_q, &bars[C::kBarQFull + w], 0,
+                                q0, h, b);
                 }
             }
             for (int t = 0; t < p.n_kt; ++t, ++g) {
@@ -254,10 +255,8 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                     mbar_arrive_expect_tx(full, C::kStageTx + (kBiasTma ? C::kBiasBytes : 0));
                     for (int w = 0; w < NWG; ++w) {
                         const int b = grp * NWG + w;
-                        tma_load_3d(stage + C::kOffK + w * C::kTile, &tm_k, full, 0, j0,
-                                    b * p.H + h);
-                        tma_load_3d(stage + C::kOffV + w * C::kTile, &tm_v, full, 0, j0,
-                                    b * p.H + h);
+                        tma_load_4d(stage + C::kOffK + w * C::kTile, &tm_k, full, 0, j0, h, b);
+                        tma_load_4d(stage + C::kOffV + w * C::kTile, &tm_v, full, 0, j0, h, b);
                     }
                     if constexpr (kBiasTma) {
                         tma_load_3d(stage + C::kOffBias, &tm_bias, full, j0, q0, h);
@@ -589,7 +588,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                 const float inv = 1.0f / fmaxf(l_run, 1e-30f);
                 if (b < p.N && row < p.Sq) {
                     const int64_t orow = (static_cast<int64_t>(b) * p.H + h) * p.Sq + row;
-                    uint16_t* dst = p.out + orow * D;
+                    uint16_t* dst = p.out + b * p.ob + h * p.oh + row * p.os;
 #pragma unroll
                     for (int c = 0; c < D / 8; ++c) {
                         uint32_t wv[4];
@@ -627,17 +626,13 @@ done:
 template <typename T, int D, bool kBiasTma>
 int launch_fwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                const void* v, const void* bias, const uint8_t* kmask, void* out, float* lse,
-               int N, int H, int Sq, int Sk, float scale) {
+               int N, int H, int Sq, int Sk, float scale, const RowView* views) {
     using C = FwdCfg<D>;
     using G = Geo<D>;
     CUtensorMap tq, tk, tv, tb;
-    const uint64_t row = 2ull * D;
-    CFK_TRY(make_tmap_3d(&tq, q, D, Sq, static_cast<uint64_t>(N) * H, row, row * Sq, D, kBM, 1,
-                         G::kSwizzleBytes, "attn q"));
-    CFK_TRY(make_tmap_3d(&tk, k, D, Sk, static_cast<uint64_t>(N) * H, row, row * Sk, D, kBN, 1,
-                         G::kSwizzleBytes, "attn k"));
-    CFK_TRY(make_tmap_3d(&tv, v, D, Sk, static_cast<uint64_t>(N) * H, row, row * Sk, D, kBN, 1,
-                         G::kSwizzleBytes, "attn v"));
+    CFK_TRY(make_tmap_rows(&tq, q, views[0], D, kBM, G::kSwizzleBytes, "attn q"));
+    CFK_TRY(make_tmap_rows(&tk, k, views[1], D, kBN, G::kSwizzleBytes, "attn k"));
+    CFK_TRY(make_tmap_rows(&tv, v, views[2], D, kBN, G::kSwizzleBytes, "attn v"));
     if (kBiasTma) {
         CFK_TRY(make_tmap_3d(&tb, bias, Sk, Sq, H, 2ull * Sk, 2ull * Sk * Sq, 64, kBM, 1, 128,
                              "attn bias"));
@@ -648,6 +643,9 @@ int launch_fwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
     p.kmask = kmask;
     p.bias = static_cast<const uint16_t*>(bias);
     p.out = static_cast<uint16_t*>(out);
+    p.ob = views[3].b;
+    p.oh = views[3].h;
+    p.os = views[3].s;
     p.lse = lse;
     p.N = N;
     p.H = H;
@@ -670,14 +668,14 @@ int launch_fwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
 template <typename T>
 int dispatch_fwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                  const void* v, const void* bias, const uint8_t* kmask, void* out, float* lse,
-                 int N, int H, int Sq, int Sk, int D, float scale) {
+                 int N, int H, int Sq, int Sk, int D, float scale, const RowView* views) {
     const bool bias_tma = (Sk % 8 == 0) && aligned16(bias);
 #define CFK_FWD_D(DD)                                                                              \
     if (D == DD) {                                                                                 \
         return bias_tma ? launch_fwd<T, DD, true>(st, dev, q, k, v, bias, kmask, out, lse, N, H,   \
-                                                  Sq, Sk, scale)                                   \
+                                                  Sq, Sk, scale, views)                            \
                         : launch_fwd<T, DD, false>(st, dev, q, k, v, bias, kmask, out, lse, N, H,  \
-                                                   Sq, Sk, scale);                                 \
+                                                   Sq, Sk, scale, views);                          \
     }
     CFK_FWD_D(8)
     CFK_FWD_D(16)
@@ -716,34 +714,58 @@ int check_attn_args(const char* fn, int dtype, int64_t N, int64_t H, int64_t Sq,
 
 using namespace cfk;
 
-extern "C" int cfk_attn_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* q, const void* k,
-                            const void* v, const void* bias, const uint8_t* kmask, void* out,
-                            float* lse, int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
-                            float scale) {
+namespace {
+
+int attn_fwd_entry(const char* fn, cfk_stream_t stream, cfk_dtype dtype, const void* q,
+                   const void* k, const void* v, const void* bias, const uint8_t* kmask,
+                   void* out, float* lse, int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                   float scale, const cfk_view* user_views) {
     clear_error();
-    CFK_TRY(check_attn_args("cfk_attn_fwd", dtype, N, H, Sq, Sk, D));
+    CFK_TRY(check_attn_args(fn, dtype, N, H, Sq, Sk, D));
+    static const char* const names[4] = {"q", "k", "v", "out"};
+    RowView views[4];
+    for (int t = 0; t < 4; ++t) {
+        const int64_t S = (t == 1 || t == 2) ? Sk : Sq;
+        CFK_TRY(view_of(fn, names[t], user_views ? &user_views[t] : nullptr, N, H, S, D,
+                        &views[t]));
+    }
     if (N == 0 || H == 0 || Sq == 0) {
         return CFK_OK;
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (Sk == 0) {
         // No keys: the reference's loop never runs and it writes 0 (volta_mma_attn.cu:139,265).
-        if (!out) {
-            return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_attn_fwd: null out");
+        if (!out || !aligned16(out)) {
+            return fail(CFK_ERR_INVALID_ARGUMENT, "%s: out must be non-null and 16-byte aligned",
+                        fn);
         }
-        cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(N * H * Sq * D) * 2, st);
+        cudaError_t e = cudaSuccess;
+        if (is_packed(views[3], D)) {
+            e = cudaMemsetAsync(out, 0, static_cast<size_t>(N * H * Sq * D) * 2, st);
+        } else {
+            DeviceInfo dev;
+            CFK_TRY(current_device(&dev));
+            const attn::ConvertJob job{{nullptr, nullptr, nullptr},
+                                       {out, out, out},
+                                       {N * H * Sq * D / 8, 0, 0},
+                                       {attn::row_strides(views[3], D),
+                                        attn::row_strides(views[3], D),
+                                        attn::row_strides(views[3], D)},
+                                       attn::d8_log2(static_cast<int>(D))};
+            attn::f32_to_16_kernel<__half><<<dev.num_sms * 8, 256, 0, st>>>(job);
+            CFK_TRY(check_launch("attn_fwd zero"));
+        }
         if (e == cudaSuccess && lse) {
             // lse = -inf (0xff800000) for an empty row
             e = cudaMemsetAsync(lse, 0xff, static_cast<size_t>(N * H * Sq) * 4, st);
         }
-        return e == cudaSuccess ? CFK_OK : fail(CFK_ERR_LAUNCH, "cfk_attn_fwd: memset failed");
+        return e == cudaSuccess ? CFK_OK : fail(CFK_ERR_LAUNCH, "%s: memset failed", fn);
     }
     if (!q || !k || !v || !bias || !kmask || !out) {
-        return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_attn_fwd: null buffer");
+        return fail(CFK_ERR_INVALID_ARGUMENT, "%s: null buffer", fn);
     }
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) {
-        return fail(CFK_ERR_INVALID_ARGUMENT,
-                    "cfk_attn_fwd: q, k, v and out must be 16-byte aligned");
+        return fail(CFK_ERR_INVALID_ARGUMENT, "%s: q, k, v and out must be 16-byte aligned", fn);
     }
     DeviceInfo dev;
     CFK_TRY(current_device(&dev));
@@ -751,9 +773,28 @@ extern "C" int cfk_attn_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* q,
                ? attn::dispatch_fwd<__nv_bfloat16>(st, dev, q, k, v, bias, kmask, out, lse,
                                                    static_cast<int>(N), static_cast<int>(H),
                                                    static_cast<int>(Sq), static_cast<int>(Sk),
-                                                   static_cast<int>(D), scale)
+                                                   static_cast<int>(D), scale, views)
                : attn::dispatch_fwd<__half>(st, dev, q, k, v, bias, kmask, out, lse,
                                             static_cast<int>(N), static_cast<int>(H),
                                             static_cast<int>(Sq), static_cast<int>(Sk),
-                                            static_cast<int>(D), scale);
+                                            static_cast<int>(D), scale, views);
+}
+
+} // namespace
+
+extern "C" int cfk_attn_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* q, const void* k,
+                            const void* v, const void* bias, const uint8_t* kmask, void* out,
+                            float* lse, int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                            float scale) {
+    return attn_fwd_entry("cfk_attn_fwd", stream, dtype, q, k, v, bias, kmask, out, lse, N, H,
+                          Sq, Sk, D, scale, nullptr);
+}
+
+extern "C" int cfk_attn_fwd_strided(cfk_stream_t stream, cfk_dtype dtype, const void* q,
+                                    const void* k, const void* v, const void* bias,
+                                    const uint8_t* kmask, void* out, float* lse, int64_t N,
+                                    int64_t H, int64_t Sq, int64_t Sk, int64_t D, float scale,
+                                    const cfk_view* views) {
+    return attn_fwd_entry("cfk_attn_fwd_strided", stream, dtype, q, k, v, bias, kmask, out, lse,
+                          N, H, Sq, Sk, D, scale, views);
 }

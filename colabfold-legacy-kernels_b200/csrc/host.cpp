@@ -104,9 +104,12 @@ int check_launch(const char* what) {
     return CFK_OK;
 }
 
-int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
-                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
-                 uint32_t b2, int swizzle_bytes, const char* what, bool f32) {
+namespace {
+
+// cuTensorMapEncodeTiled of a rank-3 or rank-4 map (dim 0 contiguous)
+int encode_tiled(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes,
+                 const char* what, bool f32) {
     std::call_once(g_encode_once, []() {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -136,20 +139,75 @@ int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, u
     default:
         return fail(CFK_ERR_INVALID_ARGUMENT, "%s: bad swizzle %d", what, swizzle_bytes);
     }
-    cuuint64_t dims[3] = {d0, d1, d2};
-    cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
-    cuuint32_t box[3] = {b0, b1, b2};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims,
-                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+    cuuint64_t gdims[4];
+    cuuint64_t gstrides[3];
+    cuuint32_t gbox[4];
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    for (int i = 0; i < rank; ++i) {
+        gdims[i] = dims[i];
+        gbox[i] = box[i];
+        if (i > 0) {
+            gstrides[i - 1] = strides_bytes[i - 1];
+        }
+    }
+    CUresult r = g_encode(map,
+                          f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                          static_cast<cuuint32_t>(rank), const_cast<void*>(base), gdims, gstrides,
+                          gbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         return fail(CFK_ERR_INVALID_ARGUMENT,
-                    "%s: cuTensorMapEncodeTiled failed (%d): dims %llu x %llu x %llu", what,
-                    static_cast<int>(r), static_cast<unsigned long long>(d0),
-                    static_cast<unsigned long long>(d1), static_cast<unsigned long long>(d2));
+                    "%s: cuTensorMapEncodeTiled failed (%d): dims %llu x %llu x %llu x %llu", what,
+                    static_cast<int>(r), static_cast<unsigned long long>(dims[0]),
+                    static_cast<unsigned long long>(dims[1]),
+                    static_cast<unsigned long long>(dims[2]),
+                    static_cast<unsigned long long>(rank > 3 ? dims[3] : 1));
     }
     return CFK_OK;
+}
+
+} // namespace
+
+int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                 uint32_t b2, int swizzle_bytes, const char* what, bool f32) {
+    const uint64_t dims[3] = {d0, d1, d2};
+    const uint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    const uint32_t box[3] = {b0, b1, b2};
+    return encode_tiled(map, 3, base, dims, strides, box, swizzle_bytes, what, f32);
+}
+
+int view_of(const char* fn, const char* name, const cfk_view* user, int64_t N, int64_t H,
+            int64_t S, int64_t D, RowView* out) {
+    if (!user) {
+        *out = packed_view(N, H, S, D);
+        return CFK_OK;
+    }
+    const int64_t ext[3] = {N, H, S};
+    const int64_t str[3] = {user->b, user->h, user->s};
+    const char* axis[3] = {"batch", "head", "sequence"};
+    for (int i = 0; i < 3; ++i) {
+        if (ext[i] > 1 && (str[i] <= 0 || str[i] % 8 != 0 || str[i] >= (1ll << 38))) {
+            return fail(CFK_ERR_INVALID_ARGUMENT,
+                        "%s: %s %s stride %lld must be a positive multiple of 8 elements", fn,
+                        name, axis[i], static_cast<long long>(str[i]));
+        }
+    }
+    *out = RowView{N, H, S, user->b, user->h, user->s};
+    return CFK_OK;
+}
+
+int make_tmap_rows(CUtensorMap* map, const void* base, const RowView& v, uint64_t d,
+                   uint32_t box_rows, int swizzle_bytes, const char* what) {
+    // dims (D, S, H, N); a dimension of extent 1 gets a harmless stride (its index is always 0)
+    const uint64_t dims[4] = {d, static_cast<uint64_t>(v.S), static_cast<uint64_t>(v.H),
+                              static_cast<uint64_t>(v.N)};
+    const uint64_t fallback = 2 * d;
+    const uint64_t strides[3] = {v.S > 1 ? 2 * static_cast<uint64_t>(v.s) : fallback,
+                                 v.H > 1 ? 2 * static_cast<uint64_t>(v.h) : fallback,
+                                 v.N > 1 ? 2 * static_cast<uint64_t>(v.b) : fallback};
+    const uint32_t box[4] = {static_cast<uint32_t>(d), box_rows, 1, 1};
+    return encode_tiled(map, 4, base, dims, strides, box, swizzle_bytes, what, false);
 }
 
 } // namespace cfk

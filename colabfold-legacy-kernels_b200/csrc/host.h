@@ -42,6 +42,35 @@ int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, u
                  uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
                  uint32_t b2, int swizzle_bytes, const char* what, bool f32 = false);
 
+// A [N, H, S, D] tensor of 16-bit elements whose D axis is contiguous: its extents and the
+// element strides of its batch, head and sequence axes.  A packed tensor has b = H S D,
+// h = S D, s = D; a transposed view (attention over the other residue axis, or a [N, S, H, D]
+// layout) only changes the strides.
+struct RowView {
+    int64_t N, H, S;
+    int64_t b, h, s;
+};
+
+inline RowView packed_view(int64_t N, int64_t H, int64_t S, int64_t D) {
+    return RowView{N, H, S, H * S * D, S * D, D};
+}
+
+inline bool is_packed(const RowView& v, int64_t D) {
+    return (v.S <= 1 || v.s == D) && (v.H <= 1 || v.h == v.S * D) &&
+           (v.N <= 1 || v.b == v.H * v.S * D);
+}
+
+// RowView of `user` (NULL = packed) with the checks the kernels rely on: every stride of an
+// axis longer than 1 a positive multiple of 8 elements (16 bytes, so every row starts 16-byte
+// aligned for TMA and vector access) and below 2^38.
+int view_of(const char* fn, const char* name, const cfk_view* user, int64_t N, int64_t H,
+            int64_t S, int64_t D, RowView* out);
+
+// TMA descriptor over a RowView: dims (D, S, H, N), box D x box_rows x 1 x 1, 16-bit elements,
+// out-of-bounds rows read as zero.
+int make_tmap_rows(CUtensorMap* map, const void* base, const RowView& v, uint64_t d,
+                   uint32_t box_rows, int swizzle_bytes, const char* what);
+
 // Argument checks shared by the attention entry points (dtype code, ranks, D in {8,16,32,64}).
 int check_attn_args(const char* fn, int dtype, int64_t N, int64_t H, int64_t Sq, int64_t Sk,
                     int64_t D);

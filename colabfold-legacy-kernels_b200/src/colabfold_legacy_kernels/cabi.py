@@ -40,6 +40,20 @@ _f32 = ctypes.c_float
 _int = ctypes.c_int
 _sz = ctypes.c_size_t
 
+
+
+class View(ctypes.Structure):
+    """cfk_view: element strides of the batch, head and sequence axes of a [N,H,S,D] tensor."""
+    _fields_ = [("b", _i64), ("h", _i64), ("s", _i64)]
+
+
+def views(*strides):
+    """A cfk_view array from (b, h, s) stride triples, for the *_strided entry points."""
+    return (View * len(strides))(*[View(*map(int, st)) for st in strides])
+
+
+_views = ctypes.POINTER(View)
+
 # name -> argtypes (restype is int for all but the two string getters)
 SIGNATURES = {
     "cfk_attn_fwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
@@ -49,6 +63,13 @@ SIGNATURES = {
                      _vp, _sz, _i64, _i64, _i64, _i64, _i64, _f32],
     "cfk_attn_bwd_phase": [_int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                            _vp, _vp, _vp, _sz, _i64, _i64, _i64, _i64, _i64, _f32],
+    "cfk_attn_fwd_strided": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                             _i64, _i64, _i64, _i64, _i64, _f32, _views],
+    "cfk_attn_bwd_strided": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                             _vp, _vp, _sz, _i64, _i64, _i64, _i64, _i64, _f32, _views],
+    "cfk_attn_bwd_phase_strided": [_int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                   _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _i64, _i64, _i64,
+                                   _f32, _views],
     "cfk_ln_fwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32],
     "cfk_ln_bwd_workspace_size": [_i64, _i64, ctypes.POINTER(_sz)],
     "cfk_ln_bwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64,

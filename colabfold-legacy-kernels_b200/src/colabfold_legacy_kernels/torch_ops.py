@@ -36,19 +36,46 @@ def _check(*ts):
                 raise ValueError("tensors must be contiguous")
 
 
+def _check_rows(*ts):
+    """[N,H,S,D] tensors may be views (any strides with a contiguous D axis): a transposed
+    residue axis or a [N,S,H,D] layout is passed to the kernels as strides, not copied."""
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("tensors must be on a CUDA device")
+        if t.dim() != 4 or (t.stride(3) != 1 and t.shape[3] > 1):
+            raise ValueError("q/k/v/out/dout and their gradients must be [N,H,S,D] with a "
+                             "contiguous D axis")
+
+
+def _strided(ts):
+    """None if every tensor is packed, else the cfk_view array of their strides."""
+    if all(t.is_contiguous() for t in ts):
+        return None
+    return cabi.views(*[t.stride()[:3] for t in ts])
+
+
 def attention_fwd(q, k, v, bias, kmask, scale, return_lse=True, out=None, lse=None):
-    """out [N,H,Sq,D] (and lse f32 [N,H,Sq]) of attention with pair bias and key mask."""
-    _check(q, k, v, bias, kmask)
+    """out [N,H,Sq,D] (and lse f32 [N,H,Sq]) of attention with pair bias and key mask.
+
+    q, k, v and `out` may be strided views (cfk_attn_fwd_strided), e.g. x.permute(1, 2, 0, 3)
+    of a [S, N, H, D] tensor for attention over its first axis."""
+    _check(bias, kmask)
     n, h, sq, d = q.shape
     sk = k.shape[2]
     if out is None:
-        out = torch.empty_like(q)
+        out = torch.empty((n, h, sq, d), dtype=q.dtype, device=q.device)
+    _check_rows(q, k, v, out)
     if return_lse and lse is None:
         lse = torch.empty((n, h, sq), dtype=torch.float32, device=q.device)
+    args = (_stream(q.device), _dtype_code(q), _ptr(q), _ptr(k), _ptr(v), _ptr(bias),
+            _ptr(kmask), _ptr(out), _ptr(lse) if return_lse else None, n, h, sq, sk, d,
+            float(scale))
+    views = _strided((q, k, v, out))
     with torch.cuda.device(q.device):
-        cabi.call("cfk_attn_fwd", _stream(q.device), _dtype_code(q), _ptr(q), _ptr(k), _ptr(v),
-                  _ptr(bias), _ptr(kmask), _ptr(out), _ptr(lse) if return_lse else None,
-                  n, h, sq, sk, d, float(scale))
+        if views is None:
+            cabi.call("cfk_attn_fwd", *args)
+        else:
+            cabi.call("cfk_attn_fwd_strided", *args, views)
     return (out, lse) if return_lse else out
 
 
@@ -63,24 +90,34 @@ def attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=None, g
 
     phase=None runs the whole backward; phase 0, 1 or 2 runs one of its launches
     (cfk_attn_bwd_phase), in which case `workspace` and `grads` must be passed to every phase.
+    q, k, v, out, dout and dq, dk, dv may be strided [N,H,S,D] views (cfk_attn_bwd_strided).
     """
-    _check(q, k, v, bias, kmask, out, lse, dout)
+    _check(bias, kmask, lse)
     n, h, sq, d = q.shape
     sk = k.shape[2]
     if grads is None:
-        grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
-                 torch.empty((h, sq, sk), dtype=torch.float32, device=q.device))
+        grads = tuple(torch.empty((n, h, s, d), dtype=q.dtype, device=q.device)
+                      for s in (sq, sk, sk)) + (
+                          torch.empty((h, sq, sk), dtype=torch.float32, device=q.device),)
     dq, dk, dv, dbias = grads
+    _check_rows(q, k, v, out, dout, dq, dk, dv)
+    _check(dbias)
     if workspace is None:
         workspace = attention_bwd_workspace(n, h, sq, sk, d, q.device)
     args = (_stream(q.device), _dtype_code(q), _ptr(q), _ptr(k), _ptr(v), _ptr(bias),
             _ptr(kmask), _ptr(out), _ptr(lse), _ptr(dout), _ptr(dq), _ptr(dk), _ptr(dv),
             _ptr(dbias), _ptr(workspace), workspace.numel(), n, h, sq, sk, d, float(scale))
+    views = _strided((q, k, v, out, dout, dq, dk, dv))
     with torch.cuda.device(q.device):
-        if phase is None:
-            cabi.call("cfk_attn_bwd", *args)
+        if views is None:
+            if phase is None:
+                cabi.call("cfk_attn_bwd", *args)
+            else:
+                cabi.call("cfk_attn_bwd_phase", int(phase), *args)
+        elif phase is None:
+            cabi.call("cfk_attn_bwd_strided", *args, views)
         else:
-            cabi.call("cfk_attn_bwd_phase", int(phase), *args)
+            cabi.call("cfk_attn_bwd_phase_strided", int(phase), *args, views)
     return dq, dk, dv, dbias
 
 

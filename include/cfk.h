@@ -97,6 +97,39 @@ CFK_API int cfk_attn_bwd_phase(int phase, cfk_stream_t stream, cfk_dtype dtype, 
                        void* dv, float* dbias, void* workspace, size_t workspace_bytes,
                        int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D, float scale);
 
+/* Strided ("view") forms of the three calls above (no counterpart in the reference).  Each
+ * [N,H,S,D] tensor is described by a cfk_view: the element strides of its batch, head and
+ * sequence axes, the D axis staying contiguous.  Attention over the other residue axis
+ * (triangle attention around the ending node, MSA column attention) or over a [N,S,H,D]
+ * layout then needs no transposed copy: the kernels' TMA descriptors and row addressing take
+ * the strides.  Strides of axes longer than 1 must be positive multiples of 8 elements; views
+ * NULL means packed, as above.  Output views must not overlap each other or the inputs.
+ * bias, kmask, lse, dbias and the workspace stay packed. */
+typedef struct cfk_view {
+    int64_t b, h, s;
+} cfk_view;
+
+/* views[0..3]: q, k, v, out */
+CFK_API int cfk_attn_fwd_strided(cfk_stream_t stream, cfk_dtype dtype, const void* q,
+                         const void* k, const void* v, const void* bias, const uint8_t* kmask,
+                         void* out, float* lse, int64_t N, int64_t H, int64_t Sq, int64_t Sk,
+                         int64_t D, float scale, const cfk_view* views);
+
+/* views[0..7]: q, k, v, out, dout, dq, dk, dv */
+CFK_API int cfk_attn_bwd_strided(cfk_stream_t stream, cfk_dtype dtype, const void* q,
+                         const void* k, const void* v, const void* bias, const uint8_t* kmask,
+                         const void* out, const float* lse, const void* dout, void* dq, void* dk,
+                         void* dv, float* dbias, void* workspace, size_t workspace_bytes,
+                         int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D, float scale,
+                         const cfk_view* views);
+CFK_API int cfk_attn_bwd_phase_strided(int phase, cfk_stream_t stream, cfk_dtype dtype,
+                               const void* q, const void* k, const void* v, const void* bias,
+                               const uint8_t* kmask, const void* out, const float* lse,
+                               const void* dout, void* dq, void* dk, void* dv, float* dbias,
+                               void* workspace, size_t workspace_bytes, int64_t N, int64_t H,
+                               int64_t Sq, int64_t Sk, int64_t D, float scale,
+                               const cfk_view* views);
+
 /* ------------------------------------------------------------------------------------------ */
 /* LayerNorm over the last axis: y = (x - mean) * rstd * gamma + beta,                        */
 /* rstd = 1/sqrt(var + eps).  x, y [M,C] in dtype; gamma, beta f32 [C]; statistics in f32.    */

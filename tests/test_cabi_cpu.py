@@ -99,3 +99,50 @@ def test_ln_gdp_fwd_arguments_without_device(libpath):
         cabi.call("cfk_ln_gdp_fwd", None, cabi.CFK_BF16, None, None, None, 1e-5, *args[:8], None,
                   0, 16, 128, 256)
     assert "null buffer" in e.value.message
+
+
+def test_strided_views_checked_without_device(libpath):
+    """cfk_attn_*_strided: strides of axes longer than 1 must be positive multiples of 8
+    elements (16-byte row starts for TMA and vector access); axes of extent 1 take any stride.
+    The checks run before any device call."""
+    from colabfold_legacy_kernels import cabi
+    N, H, S, D = 3, 2, 40, 32
+    packed = (H * S * D, S * D, D)
+    bad = cabi.views(packed, packed, (H * D, D, N * H * D + 4), packed)
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_attn_fwd_strided", None, cabi.CFK_BF16, None, None, None, None, None,
+                  None, None, N, H, S, S, D, 1.0, bad)
+    assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT
+    assert "v sequence stride" in e.value.message
+    neg = cabi.views(packed, packed, packed, (0, S * D, D))
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_attn_fwd_strided", None, cabi.CFK_BF16, None, None, None, None, None,
+                  None, None, N, H, S, S, D, 1.0, neg)
+    assert "out batch stride" in e.value.message
+    # extent-1 axes: any stride passes the view checks (the call then fails on null buffers)
+    one = cabi.views(*[(5, 3, D)] * 4)
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_attn_fwd_strided", None, cabi.CFK_BF16, None, None, None, None, None,
+                  None, None, 1, 1, S, S, D, 1.0, one)
+    assert "null buffer" in e.value.message
+    bwd = cabi.views(*([packed] * 7 + [(H * S * D, S * D, 12)]))
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_attn_bwd_strided", None, cabi.CFK_BF16, *([None] * 13), 0, N, H, S, S, D,
+                  1.0, bwd)
+    assert "dv sequence stride" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_attn_bwd_phase_strided", 3, None, cabi.CFK_BF16, *([None] * 13), 0, N, H,
+                  S, S, D, 1.0, None)
+    assert "phase 3" in e.value.message
+
+
+def test_torch_views_choose_the_strided_entry():
+    """torch_ops passes packed tensors to the packed entry points and [N,H,S,D] views (D
+    contiguous) as cfk_view strides; the check needs no device."""
+    import torch
+    from colabfold_legacy_kernels import torch_ops
+    x = torch.empty(7, 3, 2, 8)            # stored [S, N, H, D]
+    packed = torch.empty(3, 2, 7, 8)
+    assert torch_ops._strided([packed, packed]) is None
+    v = torch_ops._strided([packed, x.permute(1, 2, 0, 3)])
+    assert [(e.b, e.h, e.s) for e in v] == [(112, 56, 8), (16, 8, 48)]
