@@ -523,28 +523,35 @@ def bench_attention_views(dev, packed_ms, steps=10):
     ws = torch_ops.attention_bwd_workspace(n, HEADS, N_RES, N_RES, HEAD_DIM, dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+
     def step():
+        evs[0].record()
         torch_ops.attention_fwd(q, k, v, bias, kmask, scale, out=out, lse=lse)
+        evs[1].record()
         for ph in range(3):
             torch_ops.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=ws,
                                     grads=grads, phase=ph)
+            evs[2 + ph].record()
 
     for _ in range(3):
         step()
-    ts = []
+    names = ("fwd", "bwd_rowstat", "bwd_main", "bwd_convert")
+    ts, parts = [], {k: [] for k in names}
     for _ in range(steps):
         flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
         step()
-        b.record()
         torch.cuda.synchronize()
-        ts.append(a.elapsed_time(b))
-    ms = sorted(ts)[len(ts) // 2]
+        ts.append(evs[0].elapsed_time(evs[4]))
+        for i, name in enumerate(names):
+            parts[name].append(evs[i].elapsed_time(evs[i + 1]))
+    med = lambda xs: sorted(xs)[len(xs) // 2]
+    ms = med(ts)
     return {"workload": "tri_end_768 fwd+bwd: [S,N,H,D] storage viewed as [N,H,S,D]",
             "metric": METRIC, "unit": UNIT,
             "value": round(attn_flops(n, HEADS, N_RES, HEAD_DIM) / (ms * 1e-3) / 1e12, 1),
             "ms_per_step": round(ms, 4), "packed_eager_ms_per_step": round(packed_ms, 4),
+            "ms_per_launch": {name: round(med(t), 4) for name, t in parts.items()},
             "launch": "eager", "steps": steps,
             "l2": "flushed between steps (256 MB write, outside the timed events)"}
 
