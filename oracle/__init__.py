@@ -8,6 +8,8 @@ reference kernels of sokrypton/colabfold-legacy-kernels:
 * LayerNorm                              -- cuda/volta_ops.cu:40-58,
 * gated dual projection                  -- cuda/volta_ops.cu:185-207
   (and cuda/volta_gdp_wmma.cu:76-96),
+* the triangle-attention module that composes them (module.py; the reference's caller, not
+  part of the reference),
 
 plus the backward passes, which the reference does not have: they are the exact derivatives of
 those forward definitions (checked against torch.autograd in tests/test_oracle.py).
@@ -27,9 +29,9 @@ from .attention import (MASKED_LOGIT, attention_bwd, attention_fwd, attention_lo
                         attention_fwd_chunked)
 from .layer_norm import layer_norm_bwd, layer_norm_fwd
 from .gdp import gdp_bwd, gdp_fwd
-from . import configs
+from . import configs, module
 
 __all__ = [
     "MASKED_LOGIT", "attention_fwd", "attention_bwd", "attention_logits", "attention_fwd_chunked",
-    "layer_norm_fwd", "layer_norm_bwd", "gdp_fwd", "gdp_bwd", "configs",
+    "layer_norm_fwd", "layer_norm_bwd", "gdp_fwd", "gdp_bwd", "configs", "module",
 ]

@@ -109,3 +109,56 @@ def test_config_generators_shapes():
     # same seed, same tensors
     t3 = oracle.configs.make_attention_inputs(cfg2)
     assert torch.equal(t2["q"], t3["q"]) and torch.equal(t2["kmask"], t3["kmask"])
+
+
+def _module_case(n=12, c=16, heads=2, head_dim=4, seed=3):
+    p = oracle.module.make_params(c, heads, head_dim, seed=seed, dtype=torch.float64)
+    g = torch.Generator().manual_seed(seed + 1)
+    z = torch.randn(n, n, c, generator=g, dtype=torch.float64)
+    res = (torch.rand(n, generator=g) > 0.2).double()
+    res[0] = 0.0                                  # one padded residue: its row is fully masked
+    mask = res[:, None] * res[None, :]
+    return z, mask, p
+
+
+@pytest.mark.parametrize("ending", [False, True])
+def test_module_matches_the_literal_algorithms(ending):
+    """The triangle-attention module (config C1's composition of LayerNorm, projections, the
+    attention op and the gated output projection) equals an index-by-index evaluation of the
+    starting-node / ending-node algorithms, including the axis swap of the ending node."""
+    z, mask, p = _module_case()
+    got = oracle.module.triangle_attention(z, mask, p, ending=ending)
+    want = oracle.module.triangle_attention_literal(z, mask, p, ending=ending)
+    assert torch.allclose(got, want, rtol=1e-10, atol=1e-10)
+
+
+@pytest.mark.parametrize("ending", [False, True])
+def test_module_backward_composition_equals_autograd(ending):
+    """The module's gradients composed from the per-op backward restatements (the composition
+    the GPU module performs) equal torch.autograd of the float64 forward."""
+    z, mask, p = _module_case(seed=5)
+    z = z.clone().requires_grad_(True)
+    params = p.tensors()
+    for t in params:
+        t.requires_grad_(True)
+    out = oracle.module.triangle_attention(z, mask, p, ending=ending)
+    dout = torch.randn(out.shape, generator=torch.Generator().manual_seed(9), dtype=torch.float64)
+    auto = torch.autograd.grad(out, [z] + params, dout)
+    dz, grads = oracle.module.triangle_attention_bwd(z.detach(), mask, p, dout, ending=ending)
+    names = ["gamma", "beta", "w_q", "w_k", "w_v", "w_b", "w_g", "b_g", "w_o", "b_o"]
+    assert torch.allclose(dz, auto[0], rtol=1e-9, atol=1e-10)
+    for name, a in zip(names, auto[1:]):
+        assert torch.allclose(grads[name], a, rtol=1e-9, atol=1e-10), name
+
+
+def test_module_c1_fp32_close_to_fp64():
+    """Config C1 (z [128,128,128], H = 4, D = 32, seed 0) end to end: the fp32 evaluation of the
+    module stays within 1e-4 of the float64 one (relative to the output's scale)."""
+    p = oracle.module.make_params(128, 4, 32, seed=0)
+    g = torch.Generator().manual_seed(0)
+    z = torch.randn(128, 128, 128, generator=g)
+    mask = torch.ones(128, 128)
+    out64 = oracle.module.triangle_attention(z, mask, p, dtype=torch.float64)
+    out32 = oracle.module.triangle_attention(z, mask, p, dtype=torch.float32)
+    scale = float(out64.abs().max())
+    assert float((out32.double() - out64).abs().max()) <= 1e-4 * scale
