@@ -487,6 +487,7 @@ def run_ours(args, rank, world, local_rank):
     }
     if world == 1 and not args.skip_extras:
         result["attention_views"] = bench_attention_views(dev, ms_eager)
+        result["module"] = bench_module(dev, ms_eager)
         result["layernorm"] = bench_layernorm(dev, pk)
         result["gdp"] = bench_gdp(dev, pk)
     elif not args.skip_extras:
@@ -552,6 +553,50 @@ def bench_attention_views(dev, packed_ms, steps=10):
             "value": round(attn_flops(n, HEADS, N_RES, HEAD_DIM) / (ms * 1e-3) / 1e12, 1),
             "ms_per_step": round(ms, 4), "packed_eager_ms_per_step": round(packed_ms, 4),
             "ms_per_launch": {name: round(med(t), 4) for name, t in parts.items()},
+            "launch": "eager", "steps": steps,
+            "l2": "flushed between steps (256 MB write, outside the timed events)"}
+
+
+def bench_module(dev, attn_ms, steps=10):
+    """The triangle-attention module (modules.TriangleAttention: LayerNorm, projections, gated
+    attention, output projection) forward + backward on a C3-sized pair representation
+    z [768, 768, 128] with 5 % padded residues, around the starting and the ending node.  Eager,
+    L2 flushed between steps; `attention_kernels_ms` is the packed attention step of the same
+    run, so the rest is the module's LayerNorm, GEMMs and elementwise work."""
+    import torch
+    from colabfold_legacy_kernels.modules import TriangleAttention
+
+    g = torch.Generator(device=dev).manual_seed(2)
+    z = torch.randn(N_RES, N_RES, 128, device=dev, generator=g).bfloat16().requires_grad_(True)
+    res = (torch.rand(N_RES, device=dev, generator=g) >= 0.05).float()
+    mask = res[:, None] * res[None, :]
+    m = TriangleAttention(128, HEADS, HEAD_DIM, device=dev)
+    dout = torch.randn(N_RES, N_RES, 128, device=dev, generator=g).bfloat16()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+    for ending in (False, True):
+        def step():
+            m(z, mask, ending=ending).backward(dout)
+
+        for _ in range(3):
+            step()
+        ts = []
+        for _ in range(steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            step()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        out["ending" if ending else "starting"] = round(sorted(ts)[len(ts) // 2], 4)
+    m2 = N_RES * N_RES
+    gemm = 3 * 2 * m2 * 128 * (3 * HEADS * HEAD_DIM + HEADS + 2 * HEADS * HEAD_DIM)
+    return {"workload": "triangle-attention module fwd+bwd, z [768,768,128] bf16, 5 % padded",
+            "ms_per_step": out, "attention_kernels_ms": round(attn_ms, 4),
+            "flops_per_step": attn_flops(N_RES, HEADS, N_RES, HEAD_DIM) + gemm,
+            "tflops": {k: round((attn_flops(N_RES, HEADS, N_RES, HEAD_DIM) + gemm) / (v * 1e9), 1)
+                       for k, v in out.items()},
             "launch": "eager", "steps": steps,
             "l2": "flushed between steps (256 MB write, outside the timed events)"}
 

@@ -46,6 +46,28 @@ class _LayerNorm(torch.autograd.Function):
         return dx, dgamma, dbeta, None
 
 
+class _Linear(torch.autograd.Function):
+    """y = x W (+ b) whose bias gradient is a GEMV (dy^T 1) rather than a column reduction of
+    dy, which for [590k, 128] bf16 gradients is several times slower."""
+
+    @staticmethod
+    def forward(ctx, x, w, b):
+        ctx.save_for_backward(x, w)
+        ctx.has_bias = b is not None
+        return torch.addmm(b, x, w) if b is not None else x @ w
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dx = dy @ w.t() if ctx.needs_input_grad[0] else None
+        dw = x.t() @ dy if ctx.needs_input_grad[1] else None
+        db = None
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            ones = torch.ones(dy.shape[0], 1, dtype=dy.dtype, device=dy.device)
+            db = (dy.t() @ ones).view(-1)
+        return dx, dw, db
+
+
 def _batch_first(ending):
     """Permutation of [Ni, Nj, H, D] storage into the kernels' [N, H, S, D] order."""
     return (1, 2, 0, 3) if ending else (0, 2, 1, 3)
@@ -112,14 +134,14 @@ class TriangleAttention(torch.nn.Module):
         bf = torch.bfloat16
         x = _LayerNorm.apply(z.to(bf).reshape(ni * nj, c), self.gamma, self.beta, self.eps)
         w_qkv = torch.cat([self.w_q, self.w_k, self.w_v], dim=1).to(bf)
-        qkv = (x @ w_qkv).view(ni, nj, 3, h, d)
-        b = (x @ self.w_b.to(bf)).view(ni, nj, h)
+        qkv = _Linear.apply(x, w_qkv, None).view(ni, nj, 3, h, d)
+        b = _Linear.apply(x, self.w_b.to(bf), None).view(ni, nj, h)
         # bias[h, query, key]: (x Wb)[query, key] around the starting node, [key, query] around
         # the ending node (the pair swapped with the residue axes)
         bias = b.permute(2, 1, 0) if ending else b.permute(2, 0, 1)
         keep = (mask != 0).to(torch.uint8)
         kmask = (keep.t() if ending else keep).contiguous()
         o = _Attention.apply(qkv, bias, kmask, 1.0 / math.sqrt(d), ending)
-        gate = torch.sigmoid(x @ self.w_g.to(bf) + self.b_g.to(bf))
-        out = (gate * o.view(ni * nj, h * d)) @ self.w_o.to(bf) + self.b_o.to(bf)
+        gate = torch.sigmoid(_Linear.apply(x, self.w_g.to(bf), self.b_g.to(bf)))
+        out = _Linear.apply(gate * o.view(ni * nj, h * d), self.w_o.to(bf), self.b_o.to(bf))
         return out.view(ni, nj, c)
