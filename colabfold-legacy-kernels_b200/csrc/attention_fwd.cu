@@ -15,11 +15,18 @@
 //   warpgroup w    softmax of batch row w of the item: thread r owns query row r.  It works
 //                  on each 128-key tile in two 64-key halves: loads the half's scores from
 //                  tensor memory, adds scale and bias, keeps the running max and sum, and
-//                  writes that half's P (16-bit) to its own tensor-memory columns, whose P V the
-//                  MMA warp starts while the second half is computed.  Once both halves of S are
-//                  in registers, the MMA warp may write the next tile's S.
+//                  writes that half's P (16-bit) to tensor memory, whose P V the MMA warp
+//                  starts while the second half is computed.
 //
-// Tensor memory per warpgroup (256 columns): S [128] | P half 0 [32] | P half 1 [32] | O [Dp].
+// D <= 32 runs three batch rows per item (NWG = 3, 448 threads): with the softmax latency
+// bound at this head size, a third warp per SM sub-partition hides more of it.  Tensor memory
+// then holds 160 columns per warpgroup, S [128] | O [Dp], and P half h is written over S
+// columns 32h..32h+31, which the softmax has already read.  The MMA warp therefore issues the
+// last P V of tile g-1 before S of tile g: tcgen05.mma operations issued by one thread run in
+// order, so that P V has read P before the S MMA overwrites those columns.
+// D = 64 runs one batch row per item (NWG = 1) with 256 columns, S [128] | P half 0 [32] |
+// P half 1 [32] | O [Dp]; there the MMA warp may write the next tile's S as soon as both
+// halves of S are in registers.
 //
 // Masked keys cost no per-score work in the common case: a second K=16 MMA adds
 // ones[128 x 16] * maskcol^T, where maskcol[j, 0] = -big for a masked or out-of-range key and 0
@@ -38,15 +45,18 @@ namespace {
 template <int D>
 struct FwdCfg {
     using G = Geo<D>;
-    static constexpr int NWG = (D == 64) ? 1 : 2; // batch rows per item (bias reuse)
+    static constexpr int NWG = (D == 64) ? 1 : 3; // batch rows per item (bias reuse)
+    // three warpgroups: P is written over S columns already read (tensor memory budget)
+    static constexpr bool kAlias = NWG == 3;
     static constexpr int NST = 2;                 // pipeline stages of k/v/bias
     static constexpr int kThreads = NWG * 128 + 64;
     static constexpr int kProducerWarp = NWG * 4;
     static constexpr int kMmaWarp = NWG * 4 + 1;
-    static constexpr uint32_t kTmemCols = NWG == 2 ? 512 : 256;
-    static constexpr int kSCol = 0;   // S of warpgroup w at w*256
-    static constexpr int kPCol = 128; // P half h (16-bit pairs, 32 columns) at w*256 + 128 + 32h
-    static constexpr int kOCol = 192; // O accumulator (Dp columns) at w*256 + 192
+    static constexpr uint32_t kTmemCols = NWG == 1 ? 256 : 512;
+    static constexpr int kWgCols = kAlias ? 160 : 256; // tensor-memory columns per warpgroup
+    static constexpr int kSCol = 0;                  // S of warpgroup w at w*kWgCols
+    static constexpr int kPCol = kAlias ? 0 : 128;   // P half h (16-bit pairs, 32 cols) at +32h
+    static constexpr int kOCol = kAlias ? 128 : 192; // O accumulator (Dp columns)
 
     static constexpr int kTile = ((G::kTileAlloc + 1023) / 1024) * 1024;
     static constexpr int kBiasBytes = 128 * 128 * 2;
@@ -78,7 +88,8 @@ struct FwdCfg {
     static constexpr int kOffAbort = kOffTmemSlot + 4;
     static constexpr int kSmemBytes = kOffAbort + 4 + 1024; // + alignment slack
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
-    static_assert(kOCol + G::kDp <= 256, "tensor memory budget");
+    static_assert(kOCol + G::kDp <= kWgCols && NWG * kWgCols <= int(kTmemCols),
+                  "tensor memory budget");
 
     static constexpr uint32_t kStageTx = 2 * NWG * G::kTileBytes; // + bias when by TMA
 };
@@ -308,8 +319,8 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                 tc_fence_after();
                 const uint32_t vb = sbase + C::kOffStages + (gp % NST) * C::kStageBytes +
                                     C::kOffV + w * C::kTile;
-                const uint32_t p_tm = tmem + w * 256 + C::kPCol + 32 * hf;
-                const uint32_t o_tm = tmem + w * 256 + C::kOCol;
+                const uint32_t p_tm = tmem + w * C::kWgCols + C::kPCol + 32 * hf;
+                const uint32_t o_tm = tmem + w * C::kWgCols + C::kOCol;
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks) {
                     umma_ts(o_tm, p_tm + ks * 8, G::mnmajor(vb, 4 * hf + ks), kIdPV,
@@ -336,11 +347,17 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                     tc_fence_after();
                     const uint32_t stage = sbase + C::kOffStages + s * C::kStageBytes;
                     for (int w = 0; w < NWG; ++w) {
-                        if (g > 0 && !mbar_wait_s(BAR(C::kBarSFree + w), (g - 1) & 1, abort_s)) {
+                        if constexpr (C::kAlias) {
+                            // S(g) overwrites P(g-1): its last P V goes first (in-order pipe)
+                            if (g > 0 && !issue_pv(w, g - 1, 1, prev_first)) {
+                                goto done;
+                            }
+                        } else if (g > 0 &&
+                                   !mbar_wait_s(BAR(C::kBarSFree + w), (g - 1) & 1, abort_s)) {
                             goto done;
                         }
                         tc_fence_after();
-                        const uint32_t s_tm = tmem + w * 256 + C::kSCol;
+                        const uint32_t s_tm = tmem + w * C::kWgCols + C::kSCol;
                         const uint32_t qb = sbase + C::kOffQ + w * C::kTile;
                         const uint32_t kb = stage + C::kOffK + w * C::kTile;
 #pragma unroll
@@ -358,9 +375,11 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                         }
                     }
                     if (g > 0) {
-                        for (int w = 0; w < NWG; ++w) {
-                            if (!issue_pv(w, g - 1, 1, prev_first)) {
-                                goto done;
+                        if constexpr (!C::kAlias) {
+                            for (int w = 0; w < NWG; ++w) {
+                                if (!issue_pv(w, g - 1, 1, prev_first)) {
+                                    goto done;
+                                }
                             }
                         }
                         umma_commit(&bars[C::kBarKvEmpty + (g - 1) % NST]);
@@ -387,9 +406,9 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
         const int w = warp >> 2;
         const int r = static_cast<int>(warp_lane_base()) + lane; // query row within the tile
         const uint32_t lane_off = warp_lane_base() << 16;
-        const uint32_t s_tm = tmem + lane_off + w * 256 + C::kSCol;
-        const uint32_t p_tm = tmem + lane_off + w * 256 + C::kPCol;
-        const uint32_t o_tm = tmem + lane_off + w * 256 + C::kOCol;
+        const uint32_t s_tm = tmem + lane_off + w * C::kWgCols + C::kSCol;
+        const uint32_t p_tm = tmem + lane_off + w * C::kWgCols + C::kPCol;
+        const uint32_t o_tm = tmem + lane_off + w * C::kWgCols + C::kOCol;
         const uint32_t flag_s = sbase + C::kOffFlag;
         const float scale = p.scale;
         const float2 scale2 = make_float2(scale, scale);
@@ -435,7 +454,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                             x[32 + i] = __uint_as_float(v[i]);
                         }
                     }
-                    if (hf == 1) {
+                    if (!C::kAlias && hf == 1) {
                         // all of S is in registers: the MMA may write the next tile's S
                         tc_fence_before();
                         __syncwarp();
