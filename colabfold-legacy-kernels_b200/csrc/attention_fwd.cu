@@ -18,15 +18,17 @@
 //                  writes that half's P (16-bit) to tensor memory, whose P V the MMA warp
 //                  starts while the second half is computed.
 //
-// D <= 32 runs three batch rows per item (NWG = 3, 448 threads): with the softmax latency
-// bound at this head size, a third warp per SM sub-partition hides more of it.  Tensor memory
-// then holds 160 columns per warpgroup, S [128] | O [Dp], and P half h is written over S
-// columns 32h..32h+31, which the softmax has already read.  The MMA warp therefore issues the
-// last P V of tile g-1 before S of tile g: tcgen05.mma operations issued by one thread run in
-// order, so that P V has read P before the S MMA overwrites those columns.
-// D = 64 runs one batch row per item (NWG = 1) with 256 columns, S [128] | P half 0 [32] |
-// P half 1 [32] | O [Dp]; there the MMA warp may write the next tile's S as soon as both
-// halves of S are in registers.
+// Batch rows per item: D = 64 runs one (NWG = 1).  D <= 32 runs three (NWG = 3, 448 threads)
+// when there are enough items to fill the SMs, else two (NWG = 2, 320 threads; see
+// rows_per_item): the softmax is latency bound at these head sizes, and a third warp per SM
+// sub-partition hides more of it.
+//
+// Tensor memory with NWG = 3: 160 columns per warpgroup, S [128] | O [Dp], and P half h is
+// written over S columns 32h..32h+31, which the softmax has already read.  The MMA warp
+// therefore issues the last P V of tile g-1 before S of tile g: tcgen05.mma operations issued
+// by one thread run in order, so that P V has read P before the S MMA overwrites those columns.
+// With NWG <= 2: 256 columns per warpgroup, S [128] | P half 0 [32] | P half 1 [32] | O [Dp];
+// there the MMA warp may write the next tile's S as soon as both halves of S are in registers.
 //
 // Masked keys cost no per-score work in the common case: a second K=16 MMA adds
 // ones[128 x 16] * maskcol^T, where maskcol[j, 0] = -big for a masked or out-of-range key and 0
@@ -42,10 +44,11 @@ namespace cfk {
 namespace attn {
 namespace {
 
-template <int D>
+template <int D, int NW>
 struct FwdCfg {
     using G = Geo<D>;
-    static constexpr int NWG = (D == 64) ? 1 : 3; // batch rows per item (bias reuse)
+    static constexpr int NWG = NW; // batch rows per item (bias reuse), one warpgroup each
+    static_assert((D == 64 && NW == 1) || (D < 64 && (NW == 2 || NW == 3)), "rows per item");
     // three warpgroups: P is written over S columns already read (tensor memory budget)
     static constexpr bool kAlias = NWG == 3;
     static constexpr int NST = 2;                 // pipeline stages of k/v/bias
@@ -107,13 +110,13 @@ struct FwdParams {
     uint32_t mask_bits;   // bf16 bits of -big, or 0 when masked keys are excluded by select
 };
 
-template <typename T, int D, bool kBiasTma>
-__global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
+template <typename T, int D, int NW, bool kBiasTma>
+__global__ void __launch_bounds__(FwdCfg<D, NW>::kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_bias, const FwdParams p) {
-    using C = FwdCfg<D>;
+    using C = FwdCfg<D, NW>;
     using G = Geo<D>;
     using E = Elem<T>;
     constexpr int NWG = C::NWG;
@@ -642,11 +645,11 @@ done:
     }
 }
 
-template <typename T, int D, bool kBiasTma>
+template <typename T, int D, int NW, bool kBiasTma>
 int launch_fwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                const void* v, const void* bias, const uint8_t* kmask, void* out, float* lse,
                int N, int H, int Sq, int Sk, float scale, const RowView* views) {
-    using C = FwdCfg<D>;
+    using C = FwdCfg<D, NW>;
     using G = Geo<D>;
     CUtensorMap tq, tk, tv, tb;
     CFK_TRY(make_tmap_rows(&tq, q, views[0], D, kBM, G::kSwizzleBytes, "attn q"));
@@ -676,7 +679,7 @@ int launch_fwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
     p.items = static_cast<int64_t>(p.n_groups) * H * p.n_qt;
     p.scale = scale;
     p.mask_bits = mask_bias_bits(scale);
-    auto kern = attn_fwd_kernel<T, D, kBiasTma>;
+    auto kern = attn_fwd_kernel<T, D, NW, kBiasTma>;
     CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, C::kSmemBytes,
                              "attn_fwd"));
     const int grid = static_cast<int>(std::min<int64_t>(p.items, dev.num_sms));
@@ -684,23 +687,44 @@ int launch_fwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
     return check_launch("attn_fwd");
 }
 
+// Batch rows per work item for D <= 32.  Three warpgroups run a row about 2 % faster than two
+// (measured at tri-768), but an item then holds more rows, so with few items per SM the last
+// wave of items leaves more SMs idle.  Pick the smaller estimate of waves x rows x cost.
+int rows_per_item(int N, int H, int Sq, int num_sms) {
+    const auto cost = [&](int nw, double per_row) {
+        const int64_t items = static_cast<int64_t>((N + nw - 1) / nw) * H * ((Sq + kBM - 1) / kBM);
+        const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(items, num_sms));
+        return static_cast<double>((items + grid - 1) / grid) * nw * per_row;
+    };
+    return cost(3, 0.982) < cost(2, 1.0) ? 3 : 2;
+}
+
 template <typename T>
 int dispatch_fwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                  const void* v, const void* bias, const uint8_t* kmask, void* out, float* lse,
                  int N, int H, int Sq, int Sk, int D, float scale, const RowView* views) {
     const bool bias_tma = (Sk % 8 == 0) && aligned16(bias);
+    const int nw = D == 64 ? 1 : rows_per_item(N, H, Sq, dev.num_sms);
+#define CFK_FWD_L(DD, NN)                                                                          \
+    return bias_tma ? launch_fwd<T, DD, NN, true>(st, dev, q, k, v, bias, kmask, out, lse, N, H,   \
+                                                  Sq, Sk, scale, views)                            \
+                    : launch_fwd<T, DD, NN, false>(st, dev, q, k, v, bias, kmask, out, lse, N, H,  \
+                                                   Sq, Sk, scale, views);
 #define CFK_FWD_D(DD)                                                                              \
     if (D == DD) {                                                                                 \
-        return bias_tma ? launch_fwd<T, DD, true>(st, dev, q, k, v, bias, kmask, out, lse, N, H,   \
-                                                  Sq, Sk, scale, views)                            \
-                        : launch_fwd<T, DD, false>(st, dev, q, k, v, bias, kmask, out, lse, N, H,  \
-                                                   Sq, Sk, scale, views);                          \
+        if (nw == 3) {                                                                             \
+            CFK_FWD_L(DD, 3)                                                                       \
+        }                                                                                          \
+        CFK_FWD_L(DD, 2)                                                                           \
     }
     CFK_FWD_D(8)
     CFK_FWD_D(16)
     CFK_FWD_D(32)
-    CFK_FWD_D(64)
+    if (D == 64) {
+        CFK_FWD_L(64, 1)
+    }
 #undef CFK_FWD_D
+#undef CFK_FWD_L
     return fail(CFK_ERR_INVALID_ARGUMENT, "cfk_attn_fwd: head dim %d not in {8,16,32,64}", D);
 }
 

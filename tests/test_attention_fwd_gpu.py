@@ -121,3 +121,24 @@ def test_fwd_large_bias_rows_select_path(cuda_device):
     kmask[:, 5] = 0
     kmask[:, 129] = 0
     _check(q, k, v, bias, kmask, 0.25, "select path")
+
+
+def _rows_per_item(n, h, sq, sms):
+    """The forward's choice of batch rows per work item for D <= 32 (rows_per_item in
+    attention_fwd.cu): three when their estimated waves x rows x cost is lower, else two."""
+    def cost(nw, per_row):
+        items = (n + nw - 1) // nw * h * ((sq + 127) // 128)
+        grid = max(1, min(items, sms))
+        return (items + grid - 1) // grid * nw * per_row
+    return 3 if cost(3, 0.982) < cost(2, 1.0) else 2
+
+
+@pytest.mark.parametrize("d", [8, 16, 32])
+def test_fwd_three_rows_per_item(cuda_device, d):
+    """Enough batch rows that the kernel runs three per work item (P written over S in tensor
+    memory), including an odd last group (602 = 3 * 200 + 2) and ragged keys."""
+    n, h, sq, sk = 602, 4, 128, 136
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert _rows_per_item(n, h, sq, sms) == 3
+    q, k, v, bias, kmask = _inputs(n, h, sq, sk, d, torch.bfloat16, seed=40 + d)
+    _check(q, k, v, bias, kmask, 1.0 / math.sqrt(d), "three rows per item, d=%d" % d)
