@@ -1,4 +1,5 @@
-"""Triangle attention (around the starting or the ending node) built on the sm_100a kernels.
+"""The Evoformer's attention modules built on the sm_100a kernels: triangle attention (around
+the starting or the ending node), MSA row attention with pair bias, MSA column attention.
 
 The reference ships the three kernels; ColabFold composes them into the Evoformer's triangle
 attention (AlphaFold 2 supplement, Algorithms 13 and 14):
@@ -13,10 +14,10 @@ This module runs that composition forward and backward on a B200:
   one for the gate (cuBLAS through torch, bf16 with f32 accumulation).
 * Attention forward/backward: cfk_attn_fwd_strided / cfk_attn_bwd_strided.  q, k, v are views
   of the projection buffer and the output is written straight into [Ni, Nj, H, D] storage, for
-  both node types (around the ending node the batch axis is the second residue axis, which is
-  just other strides), so no transposed copy of q, k, v, o or of their gradients is made; dq, dk
-  and dv land in views of one [Ni, Nj, 3, H, D] gradient buffer that feeds the projection's
-  weight gradient directly.
+  attention along either axis (around the ending node, or along an MSA column, the batch axis
+  is the second axis, which is just other strides), so no transposed copy of q, k, v, o or of
+  their gradients is made; dq, dk and dv land in views of one [Ni, Nj, 3, H, D] gradient
+  buffer that feeds the projection's weight gradient directly.
 * The gate and the output projection: torch elementwise ops and a cuBLAS GEMM.
 
 Activations are bf16; LayerNorm's gamma and beta are f32 (the kernels' contract); the weights are
@@ -102,15 +103,25 @@ class _Attention(torch.autograd.Function):
         return dqkv, dbias.to(bias.dtype), None, None, None
 
 
-class TriangleAttention(torch.nn.Module):
-    """Gated triangle self-attention over a pair representation z [Ni, Nj, C].
+def _gated_attention(x, a, b, heads, head_dim, w_qkv, w_g, b_g, w_o, b_o, bias, kmask,
+                     over_first):
+    """Gated attention over one axis of normalised rows x [a*b, C] (bf16) laid out [a, b, C]:
+    over the second axis (batch = first axis) or, with over_first, over the first (batch =
+    second axis).  bias [H, S, S] bf16 (S = the attended axis' length), kmask u8 [batch, S].
+    Returns [a*b, C_out]."""
+    bf = torch.bfloat16
+    qkv = _Linear.apply(x, w_qkv.to(bf), None).view(a, b, 3, heads, head_dim)
+    o = _Attention.apply(qkv, bias, kmask, 1.0 / math.sqrt(head_dim), over_first)
+    gate = torch.sigmoid(_Linear.apply(x, w_g.to(bf), b_g.to(bf)))
+    return _Linear.apply(gate * o.view(a * b, heads * head_dim), w_o.to(bf), b_o.to(bf))
 
-    forward(z, mask, ending=False): mask [Ni, Nj] (nonzero = keep) masks the keys of each
-    attention row; ending=False attends along j for every i (starting node), ending=True along
-    i for every j (ending node).  Returns [Ni, Nj, C] in bf16.
-    """
 
-    def __init__(self, c=128, heads=4, head_dim=32, eps=1e-5, device=None):
+class _GatedAttentionParams(torch.nn.Module):
+    """LayerNorm and gated-attention parameters (f32 master copies): gamma, beta, w_q, w_k,
+    w_v, w_g, b_g, w_o, b_o.  The gate starts open (b_g = 1) and the output at zero (w_o = 0),
+    as in AlphaFold."""
+
+    def __init__(self, c, heads, head_dim, eps, device):
         super().__init__()
         hd = heads * head_dim
         f32 = dict(dtype=torch.float32, device=device)
@@ -120,28 +131,92 @@ class TriangleAttention(torch.nn.Module):
         self.w_q = torch.nn.Parameter(torch.randn(c, hd, **f32) * c ** -0.5)
         self.w_k = torch.nn.Parameter(torch.randn(c, hd, **f32) * c ** -0.5)
         self.w_v = torch.nn.Parameter(torch.randn(c, hd, **f32) * c ** -0.5)
-        self.w_b = torch.nn.Parameter(torch.randn(c, heads, **f32) * c ** -0.5)
         self.w_g = torch.nn.Parameter(torch.zeros(c, hd, **f32))
         self.b_g = torch.nn.Parameter(torch.ones(hd, **f32))
         self.w_o = torch.nn.Parameter(torch.zeros(hd, c, **f32))
         self.b_o = torch.nn.Parameter(torch.zeros(c, **f32))
 
+    def _norm(self, t):
+        a, b, c = t.shape
+        return _LayerNorm.apply(t.to(torch.bfloat16).reshape(a * b, c), self.gamma, self.beta,
+                                self.eps)
+
+    def _attend(self, x, a, b, bias, kmask, over_first):
+        w_qkv = torch.cat([self.w_q, self.w_k, self.w_v], dim=1)
+        return _gated_attention(x, a, b, self.heads, self.head_dim, w_qkv, self.w_g, self.b_g,
+                                self.w_o, self.b_o, bias, kmask, over_first)
+
+
+class TriangleAttention(_GatedAttentionParams):
+    """Gated triangle self-attention over a pair representation z [Ni, Nj, C].
+
+    forward(z, mask, ending=False): mask [Ni, Nj] (nonzero = keep) masks the keys of each
+    attention row; ending=False attends along j for every i (starting node), ending=True along
+    i for every j (ending node).  Returns [Ni, Nj, C] in bf16.
+    """
+
+    def __init__(self, c=128, heads=4, head_dim=32, eps=1e-5, device=None):
+        super().__init__(c, heads, head_dim, eps, device)
+        self.w_b = torch.nn.Parameter(
+            torch.randn(c, heads, dtype=torch.float32, device=device) * c ** -0.5)
+
     def forward(self, z, mask, ending=False):
         ni, nj, c = z.shape
         if ni != nj or mask.shape != (ni, nj):
             raise ValueError("triangle attention needs a square pair representation and mask")
-        h, d = self.heads, self.head_dim
-        bf = torch.bfloat16
-        x = _LayerNorm.apply(z.to(bf).reshape(ni * nj, c), self.gamma, self.beta, self.eps)
-        w_qkv = torch.cat([self.w_q, self.w_k, self.w_v], dim=1).to(bf)
-        qkv = _Linear.apply(x, w_qkv, None).view(ni, nj, 3, h, d)
-        b = _Linear.apply(x, self.w_b.to(bf), None).view(ni, nj, h)
+        x = self._norm(z)
+        b = _Linear.apply(x, self.w_b.to(torch.bfloat16), None).view(ni, nj, self.heads)
         # bias[h, query, key]: (x Wb)[query, key] around the starting node, [key, query] around
         # the ending node (the pair swapped with the residue axes)
         bias = b.permute(2, 1, 0) if ending else b.permute(2, 0, 1)
         keep = (mask != 0).to(torch.uint8)
         kmask = (keep.t() if ending else keep).contiguous()
-        o = _Attention.apply(qkv, bias, kmask, 1.0 / math.sqrt(d), ending)
-        gate = torch.sigmoid(_Linear.apply(x, self.w_g.to(bf), self.b_g.to(bf)))
-        out = _Linear.apply(gate * o.view(ni * nj, h * d), self.w_o.to(bf), self.b_o.to(bf))
-        return out.view(ni, nj, c)
+        return self._attend(x, ni, nj, bias, kmask, ending).view(ni, nj, c)
+
+
+class MSARowAttentionWithPairBias(_GatedAttentionParams):
+    """Gated self-attention along the residues of each MSA row, biased by the pair
+    representation (AlphaFold 2 supplement, Algorithm 7).
+
+    forward(m, z, msa_mask): m [S, R, C_m], z [R, R, C_z], msa_mask [S, R].  The bias is
+    LayerNorm(z) W_b, [H, R, R], shared by all S rows.  Returns [S, R, C_m] in bf16.
+    """
+
+    def __init__(self, c_m=64, c_z=128, heads=8, head_dim=8, eps=1e-5, device=None):
+        super().__init__(c_m, heads, head_dim, eps, device)
+        f32 = dict(dtype=torch.float32, device=device)
+        self.gamma_z = torch.nn.Parameter(torch.ones(c_z, **f32))
+        self.beta_z = torch.nn.Parameter(torch.zeros(c_z, **f32))
+        self.w_b = torch.nn.Parameter(torch.randn(c_z, heads, **f32) * c_z ** -0.5)
+
+    def forward(self, m, z, msa_mask):
+        s, r, c = m.shape
+        if z.shape[:2] != (r, r) or msa_mask.shape != (s, r):
+            raise ValueError("m [S,R,C], z [R,R,Cz] and msa_mask [S,R] disagree")
+        x = self._norm(m)
+        zn = _LayerNorm.apply(z.to(torch.bfloat16).reshape(r * r, z.shape[2]), self.gamma_z,
+                              self.beta_z, self.eps)
+        bias = _Linear.apply(zn, self.w_b.to(torch.bfloat16), None).view(r, r, self.heads)
+        kmask = (msa_mask != 0).to(torch.uint8).contiguous()
+        return self._attend(x, s, r, bias.permute(2, 0, 1), kmask, False).view(s, r, c)
+
+
+class MSAColumnAttention(_GatedAttentionParams):
+    """Gated self-attention along the sequences of each MSA column (AlphaFold 2 supplement,
+    Algorithm 8): the batch is the residue axis, read through strides, and there is no pair
+    bias (the kernel gets a zero bias).
+
+    forward(m, msa_mask): m [S, R, C_m], msa_mask [S, R].  Returns [S, R, C_m] in bf16.
+    """
+
+    def __init__(self, c_m=64, heads=8, head_dim=8, eps=1e-5, device=None):
+        super().__init__(c_m, heads, head_dim, eps, device)
+
+    def forward(self, m, msa_mask):
+        s, r, c = m.shape
+        if msa_mask.shape != (s, r):
+            raise ValueError("m [S,R,C] and msa_mask [S,R] disagree")
+        x = self._norm(m)
+        bias = torch.zeros((self.heads, s, s), dtype=torch.bfloat16, device=m.device)
+        kmask = (msa_mask != 0).to(torch.uint8).t().contiguous()
+        return self._attend(x, s, r, bias, kmask, True).view(s, r, c)

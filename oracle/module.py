@@ -182,3 +182,124 @@ def triangle_attention_bwd(z, mask, p, dout, ending=False, dtype=torch.float64):
     dz, grads["gamma"], grads["beta"] = layer_norm_bwd(z2, gamma, dx.reshape(-1, c), p.eps, mean,
                                                        rstd, dtype)
     return dz.view(ni, nj, c), grads
+
+
+# ------------------------------------------------------------------------------------------
+# MSA row attention with pair bias and MSA column attention (AlphaFold 2 supplement,
+# Algorithms 7 and 8): the same gated attention over one axis of m [S, R, C_m].
+# ------------------------------------------------------------------------------------------
+
+@dataclass
+class MsaAttnParams:
+    gamma: torch.Tensor  # [C_m]
+    beta: torch.Tensor
+    w_q: torch.Tensor    # [C_m, H*D]
+    w_k: torch.Tensor
+    w_v: torch.Tensor
+    w_g: torch.Tensor
+    b_g: torch.Tensor    # [H*D]
+    w_o: torch.Tensor    # [H*D, C_m]
+    b_o: torch.Tensor    # [C_m]
+    heads: int
+    gamma_z: torch.Tensor = None  # row attention only: LayerNorm of z and the bias weights
+    beta_z: torch.Tensor = None
+    w_b: torch.Tensor = None      # [C_z, H]
+    eps: float = 1e-5
+
+    NAMES = ("gamma", "beta", "w_q", "w_k", "w_v", "w_g", "b_g", "w_o", "b_o")
+    PAIR_NAMES = ("gamma_z", "beta_z", "w_b")
+
+    def named(self):
+        names = self.NAMES + (self.PAIR_NAMES if self.w_b is not None else ())
+        return [(n, getattr(self, n)) for n in names]
+
+
+def make_msa_params(c_m=64, heads=8, head_dim=8, c_z=None, seed=0, dtype=torch.float32):
+    """Random parameters (LayerNorm gamma = 1 + 0.1 N, beta = 0.1 N; weights N(0, 1/fan-in);
+    gate bias 1 + 0.1 N, output bias 0.1 N); c_z given = with the pair-bias branch."""
+    g = torch.Generator().manual_seed(seed)
+    hd = heads * head_dim
+
+    def rn(*shape, std=1.0):
+        return (torch.randn(*shape, generator=g) * std).to(dtype)
+
+    p = MsaAttnParams(gamma=1.0 + rn(c_m, std=0.1), beta=rn(c_m, std=0.1),
+                      w_q=rn(c_m, hd, std=c_m ** -0.5), w_k=rn(c_m, hd, std=c_m ** -0.5),
+                      w_v=rn(c_m, hd, std=c_m ** -0.5), w_g=rn(c_m, hd, std=c_m ** -0.5),
+                      b_g=1.0 + rn(hd, std=0.1), w_o=rn(hd, c_m, std=hd ** -0.5),
+                      b_o=rn(c_m, std=0.1), heads=heads)
+    if c_z is not None:
+        p.gamma_z, p.beta_z = 1.0 + rn(c_z, std=0.1), rn(c_z, std=0.1)
+        p.w_b = rn(c_z, heads, std=c_z ** -0.5)
+    return p
+
+
+def _gated_over_second_axis(x, p, bias, kmask, dtype):
+    """Gated attention along the second axis of x [A, B, C] (batch = first axis)."""
+    a, b, c = x.shape
+    w = {n: t.to(dtype) for n, t in p.named()}
+    hd = w["w_q"].shape[1]
+    d = hd // p.heads
+
+    def heads_first(t):
+        return t.view(a, b, p.heads, d).permute(0, 2, 1, 3)
+
+    q, k, v = (heads_first(x @ w[n]) for n in ("w_q", "w_k", "w_v"))
+    o, _ = attention_fwd(q, k, v, bias, kmask, 1.0 / math.sqrt(d), dtype)
+    o = o.permute(0, 2, 1, 3).reshape(a, b, hd)
+    gate = torch.sigmoid(x @ w["w_g"] + w["b_g"])
+    return (gate * o) @ w["w_o"] + w["b_o"]
+
+
+def _ln3(t, gamma, beta, eps, dtype):
+    a, b, c = t.shape
+    return layer_norm_fwd(t.reshape(a * b, c), gamma.to(dtype), beta.to(dtype), eps,
+                          dtype)[0].view(a, b, c)
+
+
+def msa_row_attention(m, z, mask, p, dtype=torch.float64):
+    """Algorithm 7: attention along the residues of each MSA row s, bias from LayerNorm(z).
+    m [S, R, C_m], z [R, R, C_z], mask [S, R]."""
+    x = _ln3(m, p.gamma, p.beta, p.eps, dtype)
+    zn = _ln3(z, p.gamma_z, p.beta_z, p.eps, dtype)
+    bias = (zn @ p.w_b.to(dtype)).permute(2, 0, 1)        # [H, R(query), R(key)]
+    return _gated_over_second_axis(x, p, bias, mask.to(torch.uint8), dtype)
+
+
+def msa_column_attention(m, mask, p, dtype=torch.float64):
+    """Algorithm 8: attention along the sequences of each MSA column r, no pair bias."""
+    s = m.shape[0]
+    x = _ln3(m, p.gamma, p.beta, p.eps, dtype).transpose(0, 1)      # [R, S, C]
+    bias = torch.zeros(p.heads, s, s, dtype=dtype)
+    out = _gated_over_second_axis(x.contiguous(), p, bias, mask.t().to(torch.uint8), dtype)
+    return out.transpose(0, 1)
+
+
+def msa_attention_literal(m, mask, p, z=None, column=False):
+    """Index-by-index float64 evaluation of Algorithm 7 (z given) or 8 (column=True)."""
+    m = m.double()
+    w = {n: t.double() for n, t in p.named()}
+
+    def ln(t, gamma, beta):
+        mu = t.mean(-1, keepdim=True)
+        return (t - mu) / torch.sqrt(((t - mu) ** 2).mean(-1, keepdim=True) + p.eps) * gamma + beta
+
+    x = ln(m, w["gamma"], w["beta"])
+    s, r, _ = x.shape
+    h = p.heads
+    d = w["w_q"].shape[1] // h
+    q, k, v = ((x @ w[n]).view(s, r, h, d) for n in ("w_q", "w_k", "w_v"))
+    keep = mask != 0
+    if not column:
+        b = ln(z.double(), w["gamma_z"], w["beta_z"]) @ w["w_b"]        # [R, R, H]
+        # a_sij = q_si . k_sj / sqrt(d) + b_ij over residues j of row s
+        logit = torch.einsum("sihd,sjhd->sijh", q, k) / math.sqrt(d) + b[None]
+        logit = torch.where(keep[:, None, :, None], logit, torch.full_like(logit, -1e4))
+        o = torch.einsum("sijh,sjhd->sihd", torch.softmax(logit, dim=2), v)
+    else:
+        # a_sti = q_si . k_ti / sqrt(d) over sequences t of column i
+        logit = torch.einsum("sihd,tihd->sith", q, k) / math.sqrt(d)
+        logit = torch.where(keep.t()[None, :, :, None], logit, torch.full_like(logit, -1e4))
+        o = torch.einsum("sith,tihd->sihd", torch.softmax(logit, dim=2), v)
+    gate = torch.sigmoid(x @ w["w_g"] + w["b_g"])
+    return (gate * o.reshape(s, r, h * d)) @ w["w_o"] + w["b_o"]

@@ -85,3 +85,68 @@ def test_module_makes_no_transposed_copies(cuda_device):
     torch.cuda.synchronize()
     assert calls.count("cfk_attn_fwd_strided") == 2 and calls.count("cfk_attn_bwd_strided") == 2
     assert "cfk_attn_fwd" not in calls and "cfk_attn_bwd" not in calls
+
+
+def _msa_case(column, seed):
+    g = torch.Generator().manual_seed(seed)
+    s, r, c_m, c_z = 64, 96, 64, 32
+    heads, d = (4, 8) if column else (4, 16)
+    p = oracle.module.make_msa_params(c_m, heads, d, c_z=None if column else c_z, seed=seed)
+    m = torch.randn(s, r, c_m, generator=g)
+    z = None if column else torch.randn(r, r, c_z, generator=g)
+    mask = (torch.rand(s, r, generator=g) > 0.1).float()
+    mask[:, -5:] = 0.0     # padded residues
+    mask[-3:] = 0.0        # padded sequences
+    return p, m, z, mask
+
+
+@pytest.mark.parametrize("column", [False, True])
+def test_msa_attention_modules(cuda_device, column):
+    """MSA row attention with pair bias (D = 16) and MSA column attention (D = 8, batch = the
+    residue axis through strides, zero bias) forward and backward against float64 autograd of
+    the oracle modules."""
+    from colabfold_legacy_kernels import modules
+    p, m, z, mask = _msa_case(column, seed=30 + column)
+    c_m = m.shape[2]
+    if column:
+        mod = modules.MSAColumnAttention(c_m, p.heads, p.w_q.shape[1] // p.heads, device="cuda")
+    else:
+        mod = modules.MSARowAttentionWithPairBias(c_m, z.shape[2], p.heads,
+                                                  p.w_q.shape[1] // p.heads, device="cuda")
+    with torch.no_grad():
+        for name, t in p.named():
+            getattr(mod, name).copy_(t)
+    mg = m.cuda().requires_grad_(True)
+    zg = None if column else z.cuda().requires_grad_(True)
+    out = mod(mg, mask.cuda()) if column else mod(mg, zg, mask.cuda())
+    dout = torch.randn(out.shape, generator=torch.Generator().manual_seed(3))
+    out.backward(dout.cuda().to(out.dtype))
+    torch.cuda.synchronize()
+
+    p64 = oracle.module.make_msa_params(c_m, p.heads, p.w_q.shape[1] // p.heads,
+                                        c_z=None if column else z.shape[2], seed=30 + column,
+                                        dtype=torch.float64)
+    leaves = [t.requires_grad_(True) for _, t in p64.named()]
+    m64 = m.double().requires_grad_(True)
+    if column:
+        ref = oracle.module.msa_column_attention(m64, mask, p64)
+        ins = [m64]
+    else:
+        z64 = z.double().requires_grad_(True)
+        ref = oracle.module.msa_row_attention(m64, z64, mask, p64)
+        ins = [m64, z64]
+    grads = torch.autograd.grad(ref, ins + leaves, dout.double())
+    what = "column" if column else "row"
+    assert_close_bf16(out, ref.detach(), "msa %s out" % what)
+    _normwise(mg.grad, grads[0], "msa %s dm" % what)
+    if not column:
+        _normwise(zg.grad, grads[1], "msa row dz")
+    ref_grads = {name: gref for (name, _), gref in zip(p64.named(), grads[len(ins):])}
+    if not column:
+        # d beta_z vanishes exactly (the bias gradient of every query row sums to zero over the
+        # keys), so on its own it is pure rounding noise: check it with d gamma_z as one vector
+        _normwise(torch.cat([mod.gamma_z.grad, mod.beta_z.grad]),
+                  torch.cat([ref_grads.pop("gamma_z"), ref_grads.pop("beta_z")]),
+                  "msa row d(gamma_z, beta_z)")
+    for name, gref in ref_grads.items():
+        _normwise(getattr(mod, name).grad, gref, "msa %s d%s" % (what, name))

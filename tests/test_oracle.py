@@ -162,3 +162,24 @@ def test_module_c1_fp32_close_to_fp64():
     out32 = oracle.module.triangle_attention(z, mask, p, dtype=torch.float32)
     scale = float(out64.abs().max())
     assert float((out32.double() - out64).abs().max()) <= 1e-4 * scale
+
+
+@pytest.mark.parametrize("column", [False, True])
+def test_msa_attention_modules_match_the_literal_algorithms(column):
+    """MSA row attention with pair bias and MSA column attention, composed from the oracle's
+    LayerNorm and attention, equal index-by-index evaluations of their algorithms."""
+    g = torch.Generator().manual_seed(21)
+    s, r = 7, 10
+    p = oracle.module.make_msa_params(12, 3, 4, c_z=None if column else 6, seed=4,
+                                      dtype=torch.float64)
+    m = torch.randn(s, r, 12, generator=g, dtype=torch.float64)
+    mask = (torch.rand(s, r, generator=g) > 0.25).double()
+    mask[2] = 0.0
+    if column:
+        got = oracle.module.msa_column_attention(m, mask, p)
+        want = oracle.module.msa_attention_literal(m, mask, p, column=True)
+    else:
+        z = torch.randn(r, r, 6, generator=g, dtype=torch.float64)
+        got = oracle.module.msa_row_attention(m, z, mask, p)
+        want = oracle.module.msa_attention_literal(m, mask, p, z=z)
+    assert torch.allclose(got, want, rtol=1e-10, atol=1e-10)
