@@ -38,7 +38,7 @@ NVCC_FLAGS = [
 
 # The kernels and the C ABI.  ffi_handlers.cc is built separately (needs the XLA headers).
 SOURCES = ["host.cpp", "status.cu", "layer_norm.cu", "attention_fwd.cu", "attention_bwd.cu",
-           "gdp.cu"]
+           "gdp.cu", "gate.cu"]
 
 
 def nvcc():

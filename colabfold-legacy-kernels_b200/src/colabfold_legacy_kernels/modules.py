@@ -18,7 +18,8 @@ This module runs that composition forward and backward on a B200:
   is the second axis, which is just other strides), so no transposed copy of q, k, v, o or of
   their gradients is made; dq, dk and dv land in views of one [Ni, Nj, 3, H, D] gradient
   buffer that feeds the projection's weight gradient directly.
-* The gate and the output projection: torch elementwise ops and a cuBLAS GEMM.
+* The gate: cfk_gate_fwd / cfk_gate_bwd, one fused pass each way; the output projection: a
+  cuBLAS GEMM.
 
 Activations are bf16; LayerNorm's gamma and beta are f32 (the kernels' contract); the weights are
 kept in f32 and cast to bf16 for the GEMMs, so their gradients arrive in f32.
@@ -69,6 +70,22 @@ class _Linear(torch.autograd.Function):
         return dx, dw, db
 
 
+class _Gate(torch.autograd.Function):
+    """sigmoid(g) * o with the forward and the backward each one fused pass (cfk_gate_*)."""
+
+    @staticmethod
+    def forward(ctx, g, o):
+        g, o = g.contiguous(), o.contiguous()
+        ctx.save_for_backward(g, o)
+        return torch_ops.gate_fwd(g, o)
+
+    @staticmethod
+    def backward(ctx, dy):
+        g, o = ctx.saved_tensors
+        d_o, dg = torch_ops.gate_bwd(g, o, dy.contiguous())
+        return dg, d_o
+
+
 def _batch_first(ending):
     """Permutation of [Ni, Nj, H, D] storage into the kernels' [N, H, S, D] order."""
     return (1, 2, 0, 3) if ending else (0, 2, 1, 3)
@@ -112,8 +129,9 @@ def _gated_attention(x, a, b, heads, head_dim, w_qkv, w_g, b_g, w_o, b_o, bias, 
     bf = torch.bfloat16
     qkv = _Linear.apply(x, w_qkv.to(bf), None).view(a, b, 3, heads, head_dim)
     o = _Attention.apply(qkv, bias, kmask, 1.0 / math.sqrt(head_dim), over_first)
-    gate = torch.sigmoid(_Linear.apply(x, w_g.to(bf), b_g.to(bf)))
-    return _Linear.apply(gate * o.view(a * b, heads * head_dim), w_o.to(bf), b_o.to(bf))
+    g = _Linear.apply(x, w_g.to(bf), b_g.to(bf))
+    gated = _Gate.apply(g, o.view(a * b, heads * head_dim))
+    return _Linear.apply(gated, w_o.to(bf), b_o.to(bf))
 
 
 class _GatedAttentionParams(torch.nn.Module):

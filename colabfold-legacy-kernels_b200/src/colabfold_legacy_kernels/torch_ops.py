@@ -223,3 +223,27 @@ def gdp_bwd(x, wp, bp, wg, bg, mask, dout, workspace=None, grads=None):
                   _ptr(wg), _ptr(bg), _ptr(mask), _ptr(dout), _ptr(dx), _ptr(dwp), _ptr(dbp),
                   _ptr(dwg), _ptr(dbg), _ptr(workspace), workspace.numel(), m, k, n)
     return dx, dwp, dbp, dwg, dbg
+
+
+def gate_fwd(g, o, out=None):
+    """sigmoid(g) * o in one pass (cfk_gate_fwd); g, o contiguous 16-bit tensors of one shape."""
+    _check(g, o)
+    if g.shape != o.shape or g.dtype != o.dtype:
+        raise ValueError("g and o must have the same shape and dtype")
+    y = torch.empty_like(o) if out is None else out
+    with torch.cuda.device(g.device):
+        cabi.call("cfk_gate_fwd", _stream(g.device), _dtype_code(g), _ptr(g), _ptr(o), _ptr(y),
+                  g.numel())
+    return y
+
+
+def gate_bwd(g, o, dy):
+    """(d_o, dg) of gate_fwd in one pass (cfk_gate_bwd)."""
+    _check(g, o, dy)
+    if not (g.shape == o.shape == dy.shape) or not (g.dtype == o.dtype == dy.dtype):
+        raise ValueError("g, o and dy must have the same shape and dtype")
+    d_o, dg = torch.empty_like(o), torch.empty_like(g)
+    with torch.cuda.device(g.device):
+        cabi.call("cfk_gate_bwd", _stream(g.device), _dtype_code(g), _ptr(g), _ptr(o), _ptr(dy),
+                  _ptr(d_o), _ptr(dg), g.numel())
+    return d_o, dg

@@ -130,6 +130,15 @@ CFK_API int cfk_attn_bwd_phase_strided(int phase, cfk_stream_t stream, cfk_dtype
                                int64_t Sq, int64_t Sk, int64_t D, float scale,
                                const cfk_view* views);
 
+/* The sigmoid gate of the Evoformer's attention modules, fused (no counterpart in the
+ * reference, whose caller runs it in jnp): forward y = sigmoid(g) * o; backward
+ * d_o = dy * sigmoid(g), dg = dy * o * sigmoid(g) * (1 - sigmoid(g)).  n elements of dtype
+ * each, every buffer 16-byte aligned; f32 arithmetic, each output rounded once. */
+CFK_API int cfk_gate_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* g, const void* o,
+                 void* y, int64_t n);
+CFK_API int cfk_gate_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* g, const void* o,
+                 const void* dy, void* d_o, void* dg, int64_t n);
+
 /* ------------------------------------------------------------------------------------------ */
 /* LayerNorm over the last axis: y = (x - mean) * rstd * gamma + beta,                        */
 /* rstd = 1/sqrt(var + eps).  x, y [M,C] in dtype; gamma, beta f32 [C]; statistics in f32.    */

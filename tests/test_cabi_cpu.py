@@ -146,3 +146,19 @@ def test_torch_views_choose_the_strided_entry():
     assert torch_ops._strided([packed, packed]) is None
     v = torch_ops._strided([packed, x.permute(1, 2, 0, 3)])
     assert [(e.b, e.h, e.s) for e in v] == [(112, 56, 8), (16, 8, 48)]
+
+
+def test_gate_arguments_without_device(libpath):
+    """cfk_gate_fwd / cfk_gate_bwd reject a bad dtype, a negative count and unaligned or null
+    buffers before any device call; n = 0 is a no-op."""
+    from colabfold_legacy_kernels import cabi
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_gate_fwd", None, 5, None, None, None, 8)
+    assert "dtype" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_gate_fwd", None, cabi.CFK_BF16, 16, 32, 48, -1)
+    assert "negative" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_gate_bwd", None, cabi.CFK_BF16, 16, 32, 48, 64, 72 + 2, 8)
+    assert "aligned" in e.value.message
+    assert cabi.call("cfk_gate_fwd", None, cabi.CFK_BF16, None, None, None, 0) == 0

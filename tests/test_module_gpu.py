@@ -150,3 +150,22 @@ def test_msa_attention_modules(cuda_device, column):
                   "msa row d(gamma_z, beta_z)")
     for name, gref in ref_grads.items():
         _normwise(getattr(mod, name).grad, gref, "msa %s d%s" % (what, name))
+
+
+@pytest.mark.parametrize("dtype,n", [(torch.bfloat16, 590_000 * 8 + 5), (torch.float16, 1003)])
+def test_gate_kernels_against_torch_fp32(cuda_device, dtype, n):
+    """cfk_gate_fwd / cfk_gate_bwd against a plain PyTorch fp32 evaluation of
+    y = sigmoid(g) * o and its gradients, rtol = atol = 2e-2 (16-bit outputs), including a
+    tail that is not a whole 16-byte vector."""
+    from colabfold_legacy_kernels import torch_ops
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    g = (torch.randn(n, device="cuda", generator=gen) * 3).to(dtype)
+    o = torch.randn(n, device="cuda", generator=gen).to(dtype)
+    dy = torch.randn(n, device="cuda", generator=gen).to(dtype)
+    y = torch_ops.gate_fwd(g, o)
+    d_o, dg = torch_ops.gate_bwd(g, o, dy)
+    torch.cuda.synchronize()
+    s = torch.sigmoid(g.float())
+    assert_close_bf16(y, s * o.float(), "gate y")
+    assert_close_bf16(d_o, dy.float() * s, "gate d_o")
+    assert_close_bf16(dg, dy.float() * o.float() * s * (1 - s), "gate dg")
