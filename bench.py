@@ -488,6 +488,7 @@ def run_ours(args, rank, world, local_rank):
     if world == 1 and not args.skip_extras:
         result["attention_views"] = bench_attention_views(dev, ms_eager)
         result["module"] = bench_module(dev, ms_eager)
+        result["other_attention_configs"] = bench_other_attention(dev)
         result["layernorm"] = bench_layernorm(dev, pk)
         result["gdp"] = bench_gdp(dev, pk)
     elif not args.skip_extras:
@@ -555,6 +556,64 @@ def bench_attention_views(dev, packed_ms, steps=10):
             "ms_per_launch": {name: round(med(t), 4) for name, t in parts.items()},
             "launch": "eager", "steps": steps,
             "l2": "flushed between steps (256 MB write, outside the timed events)"}
+
+
+def bench_other_attention(dev, steps=10):
+    """BASELINE's other attention configurations on one GPU, full size: C2 (MSA row attention
+    with pair bias, [512, 8, 256, 32], fwd + the three backward launches) and C5 (triangle
+    attention at N_res = 2048, forward only).  Eager launches, L2 flushed between steps."""
+    import torch
+    import oracle
+    from colabfold_legacy_kernels import torch_ops
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return sorted(ts)[len(ts) // 2]
+
+    out = {}
+    for cfg, backward in ((oracle.configs.C2, True), (oracle.configs.C5, False)):
+        t = oracle.configs.make_attention_inputs(cfg, device=dev)
+        q, k, v, bias, kmask, scale = (t[x] for x in ("q", "k", "v", "bias", "kmask", "scale"))
+        n, h, s, d = q.shape
+        o = torch.empty_like(q)
+        lse = torch.empty((n, h, s), dtype=torch.float32, device=dev)
+        if backward:
+            dout = t["dout"]
+            ws = torch_ops.attention_bwd_workspace(n, h, s, s, d, dev)
+            grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
+                     torch.empty((h, s, s), dtype=torch.float32, device=dev))
+
+            def fn():
+                torch_ops.attention_fwd(q, k, v, bias, kmask, scale, out=o, lse=lse)
+                torch_ops.attention_bwd(q, k, v, bias, kmask, o, lse, dout, scale, workspace=ws,
+                                        grads=grads)
+            flops = attn_flops(n, h, s, d)
+        else:
+            def fn():
+                torch_ops.attention_fwd(q, k, v, bias, kmask, scale, out=o, lse=lse)
+            flops = 4 * n * h * s * s * d
+        ms = timed(fn)
+        out[cfg.name] = {"shape": [n, h, s, d], "pass": "fwd+bwd" if backward else "fwd",
+                         "ms": round(ms, 4), "tflops": round(flops / (ms * 1e9), 1),
+                         "gflop": round(flops / 1e9, 1)}
+        del t, q, k, v, o, lse, fn
+        if backward:
+            del ws, grads, dout
+    out["launch"] = "eager"
+    out["l2"] = "flushed between steps (256 MB write, outside the timed events)"
+    return out
 
 
 def bench_module(dev, attn_ms, steps=10):
