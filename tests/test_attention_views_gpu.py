@@ -156,3 +156,26 @@ def test_empty_keys_and_queries_through_views(cuda_device):
     torch.cuda.synchronize()
     assert torch.all(gstore == 0)
     assert cabi.device_status() == 0
+
+
+def test_fwd_bwd_views_three_rows_per_item(cuda_device):
+    """Enough batch rows that the forward runs three per work item (602 rows, H = 4, one query
+    tile), through ending-node views: forward bit for bit as the packed call, backward against
+    the packed call."""
+    from colabfold_legacy_kernels import torch_ops
+    q, k, v, bias, kmask, dout = _ending_node(602, 4, 128, 136, 32, torch.bfloat16, seed=610)
+    out, lse = torch_ops.attention_fwd(q, k, v, bias, kmask, 0.2, out=_sndh_like(q))
+    ref, ref_lse = torch_ops.attention_fwd(q.contiguous(), k.contiguous(), v.contiguous(), bias,
+                                           kmask, 0.2)
+    grads = (_sndh_like(q), _sndh_like(k), _sndh_like(v),
+             torch.empty(bias.shape, dtype=torch.float32, device=q.device))
+    dq, dk, dv, dbias = torch_ops.attention_bwd(q, k, v, bias, kmask, out, lse, dout, 0.2,
+                                                grads=grads)
+    rq, rk, rv, rb = torch_ops.attention_bwd(q.contiguous(), k.contiguous(), v.contiguous(), bias,
+                                             kmask, ref, ref_lse, dout.contiguous(), 0.2)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref) and torch.equal(lse, ref_lse)
+    assert_close_bf16(dq, rq, "602-row view dq")
+    assert_close_bf16(dk, rk, "602-row view dk")
+    assert_close_bf16(dv, rv, "602-row view dv")
+    assert_close_f32(dbias, rb, "602-row view dbias")
