@@ -34,6 +34,17 @@ namespace {
 constexpr int kThreads = 320; // 2 epilogue warpgroups + producer warp + MMA warp
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
+
+// Forward: four epilogue warpgroups (32 output columns each per 128-column chunk); with the
+// fused LayerNorm two (64 columns each), which leaves the LayerNorm warpgroup its registers.
+template <bool kLn>
+struct FwdWarps {
+    static constexpr int kEpiWg = kLn ? 2 : 4;
+    static constexpr int kCols = 128 / kEpiWg;      // output columns per warpgroup and chunk
+    static constexpr int kProducer = 4 * kEpiWg;
+    static constexpr int kMma = kProducer + 1;
+    static constexpr int kThreads = (kMma + 1) * 32 + (kLn ? 128 : 0);
+};
 constexpr int kMaxK = 128;
 constexpr int kWeightBudget = 128 * 1024; // both weight matrices, resident
 
@@ -112,7 +123,7 @@ struct LnIn {
 // run, normalises them in f32 and writes the 16-bit result straight into the x stage in the
 // swizzled layout the MMA reads; the producer then loads only the weights.
 template <typename T, bool kLn>
-__global__ void __launch_bounds__(kLn ? kThreads + 128 : kThreads, 1)
+__global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
     gdp_fwd_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_wp,
                    const __grid_constant__ CUtensorMap tm_wg,
@@ -120,6 +131,9 @@ __global__ void __launch_bounds__(kLn ? kThreads + 128 : kThreads, 1)
                    const uint16_t* __restrict__ bg, const uint16_t* __restrict__ mask, int M,
                    int K, int N, const LnIn ln) {
     using E = Elem<T>;
+    using FW = FwdWarps<kLn>;
+    constexpr int kProducerWarp = FW::kProducer;
+    constexpr int kMmaWarp = FW::kMma;
     const FwdLayout L = fwd_layout(K, N);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -144,7 +158,7 @@ __global__ void __launch_bounds__(kLn ? kThreads + 128 : kThreads, 1)
             mbar_init(&x_full[i], 1);
             mbar_init(&x_empty[i], 1);
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 8);
+            mbar_init(&acc_empty[i], 4 * FW::kEpiWg);
             mbar_init(&x_ready[i], 4);
         }
         mbar_init(w_full, 1);
@@ -370,13 +384,18 @@ __global__ void __launch_bounds__(kLn ? kThreads + 128 : kThreads, 1)
             }
         }
     } else {
-        // epilogue: thread (w, r) owns row r and columns [64w, 64w + 64) of each chunk; the
-        // warpgroup stages its [128 x 64] box (128-byte swizzle) in shared memory and one thread
-        // writes it with a TMA store (rows >= M and columns >= N are clipped by the map)
+        // epilogue: thread (w, r) owns row r and columns [kCols w, +kCols) of each chunk; the
+        // warpgroup stages its [128 x kCols] box (2 kCols-byte swizzle) in shared memory and
+        // one thread writes it with a TMA store (rows >= M and columns >= N are clipped by the
+        // map)
+        constexpr int kCols = FW::kCols;
+        constexpr int kRowB = 2 * kCols;                 // bytes per staged row
+        constexpr int kSwz = kRowB / 16 - 1;             // 16-byte chunks per row - 1
         const int w = warp >> 2;
         const int r = static_cast<int>(attn::warp_lane_base()) + lane;
         const uint32_t lane_off = attn::warp_lane_base() << 16;
-        const uint32_t stg_row = sbase + L.off_stg + w * 16384 + r * 128;
+        const uint32_t stg_row = sbase + L.off_stg + w * 128 * kRowB + r * kRowB;
+        const int swz = ((r * kRowB) >> 7) & kSwz;
         const bool leader = (threadIdx.x == 128 * w);
         uint32_t chunk_ctr = 0;
         for (int i = 0; i < n_mine; ++i) {
@@ -396,10 +415,10 @@ __global__ void __launch_bounds__(kLn ? kThreads + 128 : kThreads, 1)
                 }
                 __syncwarp();
                 tc_fence_after();
-                const uint32_t accp = tmem + lane_off + bf * 256 + 64 * w;
+                const uint32_t accp = tmem + lane_off + bf * 256 + kCols * w;
                 const uint32_t accg = accp + 128;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < kCols / 16; ++q) {
                     uint32_t pv[16], gv[16];
                     tmem_ld16(accp + 16 * q, pv);
                     tmem_ld16(accg + 16 * q, gv);
@@ -419,9 +438,9 @@ __global__ void __launch_bounds__(kLn ? kThreads + 128 : kThreads, 1)
                         o[e] = E::pack(y[0], y[1]);
                     }
                     // columns 16q..16q+15 of the box row = 16-byte chunks 2q, 2q+1
-                    attn::sts128(stg_row + (((2 * q) ^ (r & 7)) << 4),
+                    attn::sts128(stg_row + (((2 * q) ^ swz) << 4),
                                  make_uint4(o[0], o[1], o[2], o[3]));
-                    attn::sts128(stg_row + (((2 * q + 1) ^ (r & 7)) << 4),
+                    attn::sts128(stg_row + (((2 * q + 1) ^ swz) << 4),
                                  make_uint4(o[4], o[5], o[6], o[7]));
                 }
                 tc_fence_before();
@@ -432,8 +451,8 @@ __global__ void __launch_bounds__(kLn ? kThreads + 128 : kThreads, 1)
                 fence_proxy_async_smem();
                 named_bar_sync(1 + w, 128);
                 if (leader) {
-                    tma_store_3d(&tm_out, sbase + L.off_stg + w * 16384, c * 128 + 64 * w,
-                                 mt * 128, 0);
+                    tma_store_3d(&tm_out, sbase + L.off_stg + w * 128 * kRowB,
+                                 c * 128 + kCols * w, mt * 128, 0);
                     bulk_commit();
                 }
             }
@@ -527,20 +546,21 @@ int gdp_fwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const vo
     }
     CUtensorMap tx, twp, twg, tout;
     // x [M, K]: dims (K, M, 1), box 64 x 128; weights [K, N]: dims (N, K, 1), box 64 x K;
-    // out [M, N]: dims (N, M, 1), box 64 x 128 (stores)
+    // out [M, N]: dims (N, M, 1), box kCols x 128 (stores; 64 with the fused LayerNorm, else 32)
     CFK_TRY(make_tmap_3d(&tx, ln ? ln->z : x, K, M, 1, 2ull * K, 2ull * K * M, 64, 128, 1, 128,
                          "gdp x"));
     CFK_TRY(make_tmap_3d(&twp, wp, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wp"));
     CFK_TRY(make_tmap_3d(&twg, wg, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wg"));
-    CFK_TRY(make_tmap_3d(&tout, out, N, M, 1, 2ull * N, 2ull * N * M, 64, 128, 1, 128,
-                         "gdp out"));
+    const int out_cols = ln ? FwdWarps<true>::kCols : FwdWarps<false>::kCols;
+    CFK_TRY(make_tmap_3d(&tout, out, N, M, 1, 2ull * N, 2ull * N * M, out_cols, 128, 1,
+                         2 * out_cols, "gdp out"));
     auto kern = ln ? gdp_fwd_kernel<T, true> : gdp_fwd_kernel<T, false>;
     CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
                              ln ? "gdp_fwd_ln" : "gdp_fwd"));
     const int n_mt = (M + 127) / 128;
     const int grid = std::min(n_mt, dev.num_sms);
     const LnIn none{};
-    kern<<<grid, ln ? kThreads + 128 : kThreads, L.total, st>>>(
+    kern<<<grid, ln ? FwdWarps<true>::kThreads : FwdWarps<false>::kThreads, L.total, st>>>(
         tx, twp, twg, tout, static_cast<const uint16_t*>(bp), static_cast<const uint16_t*>(bg),
         static_cast<const uint16_t*>(mask), M, K, N, ln ? *ln : none);
     return check_launch(ln ? "gdp_fwd_ln" : "gdp_fwd");
