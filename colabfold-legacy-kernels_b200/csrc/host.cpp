@@ -193,6 +193,15 @@ int view_of(const char* fn, const char* name, const cfk_view* user, int64_t N, i
                         name, axis[i], static_cast<long long>(str[i]));
         }
     }
+    // the farthest element must stay addressable: below 2^40 elements (2 TiB of 16-bit data)
+    // keeps every offset the kernels form within int64 and within the TMA's address range
+    const double last = static_cast<double>(N > 0 ? N - 1 : 0) * static_cast<double>(str[0]) +
+                        static_cast<double>(H > 0 ? H - 1 : 0) * static_cast<double>(str[1]) +
+                        static_cast<double>(S > 0 ? S - 1 : 0) * static_cast<double>(str[2]) +
+                        static_cast<double>(D);
+    if (last >= 1099511627776.0) {
+        return fail(CFK_ERR_INVALID_ARGUMENT, "%s: %s view reaches past 2^40 elements", fn, name);
+    }
     *out = RowView{N, H, S, user->b, user->h, user->s};
     return CFK_OK;
 }

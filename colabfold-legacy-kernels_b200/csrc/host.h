@@ -62,7 +62,7 @@ inline bool is_packed(const RowView& v, int64_t D) {
 
 // RowView of `user` (NULL = packed) with the checks the kernels rely on: every stride of an
 // axis longer than 1 a positive multiple of 8 elements (16 bytes, so every row starts 16-byte
-// aligned for TMA and vector access) and below 2^38.
+// aligned for TMA and vector access) and below 2^38, and the view's last element below 2^40.
 int view_of(const char* fn, const char* name, const cfk_view* user, int64_t N, int64_t H,
             int64_t S, int64_t D, RowView* out);
 

@@ -125,6 +125,11 @@ def test_strided_views_checked_without_device(libpath):
         cabi.call("cfk_attn_fwd_strided", None, cabi.CFK_BF16, None, None, None, None, None,
                   None, None, 1, 1, S, S, D, 1.0, one)
     assert "null buffer" in e.value.message
+    far = cabi.views(packed, packed, packed, ((1 << 38) - 8, S * D, D))
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_attn_fwd_strided", None, cabi.CFK_BF16, None, None, None, None, None,
+                  None, None, 16, H, S, S, D, 1.0, far)
+    assert "past 2^40" in e.value.message
     bwd = cabi.views(*([packed] * 7 + [(H * S * D, S * D, 12)]))
     with pytest.raises(cabi.CfkError) as e:
         cabi.call("cfk_attn_bwd_strided", None, cabi.CFK_BF16, *([None] * 13), 0, N, H, S, S, D,
