@@ -14,13 +14,14 @@ value      = 695.8 GFLOP (algorithmic fwd+bwd flops of the whole job) / ms_per_s
 e2e        = the same metric through the C ABI with pinned host buffers: every step copies
              q, k, v, bias, kmask, dout host->device and out, dq, dk, dv, dbias device->host
 roofline   = the dominant kernel (the backward main kernel), achieved TFLOP/s from CUDA events
-             around its launches against the measured sustained bf16 peak
+             around its launches against the measured burst bf16 peak (it runs inside a step of
+             a few ms, not a seconds-long loop)
 cpu_baseline = the CPU oracle (torch, fp32, all host threads) on a bounded sample of rows
 Also reported: LayerNorm forward HBM GB/s and the gated dual projection on config C4.
 
 --impl reference times the reference's CPU path for this workload: the reference ships GPU
 kernels for sm_70/sm_75 only and no CPU implementation, so its semantics restated on the CPU
-(oracle/, torch fp32, all host threads) stand in, on a bounded sample of rows per step.
+(oracle/, torch fp32, all host threads) stand in; every step is the whole 768-row workload.
 """
 
 import argparse
@@ -215,30 +216,36 @@ def cpu_sample_inputs(rows):
 
 
 def run_reference(args, rank):
-    """--impl reference: the CPU restatement, rank 0 only."""
+    """--impl reference: the CPU restatement, rank 0 only.  Every step is the whole C3 workload
+    (all 768 attention rows, forward + backward), so the step time is measured, not scaled."""
     if rank != 0:
         return None
-    rows = args.cpu_rows
+    rows = args.ref_rows or N_RES
     inputs = cpu_sample_inputs(rows)
-    for _ in range(max(1, args.warmup)):
-        cpu_attention_sample(inputs, rows)
+    # warm-up: one small slice (thread pools, allocator), not a whole step
+    cpu_attention_sample(cpu_sample_inputs(8), 8)
     secs = []
     flops = None
     threads = None
+    t_all = time.perf_counter()
     for _ in range(args.steps):
         t, flops, threads = cpu_attention_sample(inputs, rows)
         secs.append(t)
+    wall = time.perf_counter() - t_all
     sec = statistics.median(secs)
     value = flops / sec / 1e12
-    sample = "%d of %d attention rows of config C3 (fwd+bwd, fp32 torch on %d threads)" % (
-        rows, N_RES, threads)
+    sample = "all %d of %d attention rows of config C3 per step (fwd+bwd, fp32 torch on %d " \
+             "threads)" % (rows, N_RES, threads)
     return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": sec * 1e3 * (N_RES / rows), "higher_is_better": True,
+        "ms_per_step": sec * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "wall_s_timed": wall,
         "config": {"workload": "tri_start_768 fwd+bwd (C3)", "n_res": N_RES, "heads": HEADS,
-                   "head_dim": HEAD_DIM, "sample_rows": rows},
+                   "head_dim": HEAD_DIM, "rows_per_step": rows,
+                   "warmup_note": "one 8-row slice warms the thread pool; the W warm-up steps "
+                                  "of a whole workload each are not repeated on the CPU"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -276,8 +283,10 @@ def run_ours(args, rank, world, local_rank):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
     comm = torch.cuda.Stream(dev) if world > 1 else None
 
-    ev = {name: [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-          for name in ("step", "fwd", "bwd_main")}
+    # marks of one eager step: main stream t0 | fwd | rowstat | main | convert | t1, and the
+    # dbias all-reduce on the comm stream ar0 | ar1 (all timed from t0)
+    ev = {name: torch.cuda.Event(enable_timing=True)
+          for name in ("t0", "fwd", "rowstat", "main", "convert", "t1", "ar0", "ar1")}
 
     main_set = {"q": q, "k": k, "v": v, "dout": dout, "kmask": kmask, "bias": bias, "out": out,
                 "lse": lse, "grads": grads}
@@ -287,37 +296,42 @@ def run_ours(args, rank, world, local_rank):
         bq, bk, bv, bb, bm, bo, bl, bd, bg = (b[x] for x in ("q", "k", "v", "bias", "kmask", "out",
                                                             "lse", "dout", "grads"))
         if record:
-            ev["step"][0].record(stream)
-            ev["fwd"][0].record(stream)
+            ev["t0"].record(stream)
         torch_ops.attention_fwd(bq, bk, bv, bb, bm, scale, out=bo, lse=bl)
         if record:
-            ev["fwd"][1].record(stream)
+            ev["fwd"].record(stream)
         torch_ops.attention_bwd(bq, bk, bv, bb, bm, bo, bl, bd, scale, workspace=ws,
                                 grads=bg, phase=0)
         if record:
-            ev["bwd_main"][0].record(stream)
+            ev["rowstat"].record(stream)
         torch_ops.attention_bwd(bq, bk, bv, bb, bm, bo, bl, bd, scale, workspace=ws,
                                 grads=bg, phase=1)
         if record:
-            ev["bwd_main"][1].record(stream)
+            ev["main"].record(stream)
         if world > 1:
             # dbias is final after the main kernel: reduce it while the converts run
             comm.wait_stream(stream)
             with torch.cuda.stream(comm):
+                if record:
+                    ev["ar0"].record(comm)
                 dist.all_reduce(bg[3])
+                if record:
+                    ev["ar1"].record(comm)
         torch_ops.attention_bwd(bq, bk, bv, bb, bm, bo, bl, bd, scale, workspace=ws,
                                 grads=bg, phase=2)
+        if record:
+            ev["convert"].record(stream)
         if world > 1:
             stream.wait_stream(comm)
         if record:
-            ev["step"][1].record(stream)
+            ev["t1"].record(stream)
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    step_ms, fwd_ms, bwd_ms = [], [], []
+    marks = {name: [] for name in ev if name != "t0"}
     with ClockSampler(local_rank, dev) as clocks:
         if world > 1:
             dist.barrier()
@@ -327,9 +341,9 @@ def run_ours(args, rank, world, local_rank):
             flush.zero_()  # untimed: evicts L2 between steps
             step(record=True)
             torch.cuda.synchronize()
-            step_ms.append(ev["step"][0].elapsed_time(ev["step"][1]))
-            fwd_ms.append(ev["fwd"][0].elapsed_time(ev["fwd"][1]))
-            bwd_ms.append(ev["bwd_main"][0].elapsed_time(ev["bwd_main"][1]))
+            for name in marks:
+                if world > 1 or name not in ("ar0", "ar1"):
+                    marks[name].append(ev["t0"].elapsed_time(ev[name]))
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -367,14 +381,28 @@ def run_ours(args, rank, world, local_rank):
             if world > 1:
                 dist.barrier()
             del graph  # holds NCCL work: released before the process group goes away
-    ms = sum(step_ms) / len(step_ms)
-    ms_fwd = sum(fwd_ms) / len(fwd_ms)
-    ms_bwd = sum(bwd_ms) / len(bwd_ms)
-    ms_graph = sum(graph_ms) / len(graph_ms) if graph_ms else 0.0
+    mean = lambda xs: sum(xs) / len(xs) if xs else 0.0
+    # per-step phase durations from the marks (eager loop)
+    pairs = {"fwd": (None, "fwd"), "bwd_rowstat": ("fwd", "rowstat"),
+             "bwd_main": ("rowstat", "main"), "bwd_convert": ("main", "convert")}
+    parts = {}
+    for name, (a, b) in pairs.items():
+        parts[name] = mean([mb - (marks[a][i] if a else 0.0) for i, mb in enumerate(marks[b])])
     if world > 1:
-        t = torch.tensor([ms, ms_fwd, ms_bwd, ms_graph], device=dev)
+        parts["allreduce"] = mean([e - b for b, e in zip(marks["ar0"], marks["ar1"])])
+        # the part of the all-reduce that the convert does not hide: it ends after the convert
+        parts["allreduce_exposed"] = mean([max(0.0, e - c) for e, c in
+                                           zip(marks["ar1"], marks["convert"])])
+    ms = mean(marks["t1"])
+    ms_graph = mean(graph_ms)
+    names = sorted(parts)
+    if world > 1:
+        t = torch.tensor([ms, ms_graph] + [parts[k] for k in names], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ms_fwd, ms_bwd, ms_graph = t.tolist()
+        vals = t.tolist()
+        ms, ms_graph = vals[:2]
+        parts = dict(zip(names, vals[2:]))
+    ms_fwd, ms_bwd = parts["fwd"], parts["bwd_main"]
     ms_eager = ms
     if graph_ms:
         ms = ms_graph
@@ -455,9 +483,10 @@ def run_ours(args, rank, world, local_rank):
     achieved = bwd_flops_launch / (ms_bwd * 1e-3) / 1e12
     roofline = {
         "kernel": "attn_bwd_kernel<bf16, D=32> (cfk_attn_bwd phase 1)",
-        "bound": "tensor", "achieved": achieved, "peak": pk["bf16_sustained"],
-        "unit": "TFLOP/s", "frac": achieved / pk["bf16_sustained"],
-        "peak_source": pk["source"] + " bf16_tflops_sustained",
+        "bound": "tensor", "achieved": achieved, "peak": pk["bf16"],
+        "unit": "TFLOP/s", "frac": achieved / pk["bf16"],
+        "peak_source": pk["source"] + " bf16_tflops (burst: the kernel runs inside a step of a "
+                       "few ms)",
         "traffic": traffic_from_profiles("attn_bwd_tri768"),
         "flops_per_launch": bwd_flops_launch,
         "ms_per_launch": ms_bwd,
@@ -476,6 +505,10 @@ def run_ours(args, rank, world, local_rank):
                    "launch": ("one CUDA graph replay per step (the step captured once, the dbias "
                               "all-reduce included)" if ms_graph else "eager launches"),
                    "eager_ms_per_step": ms_eager},
+        "breakdown_ms": dict({k: round(v, 4) for k, v in parts.items()},
+                             note="eager step, mean per step, max over ranks; allreduce_exposed "
+                                  "= time the dbias all-reduce (comm stream) runs past the end "
+                                  "of the convert it overlaps"),
         "gpu_launches": 4 * args.steps,  # attn_fwd, rowstat, attn_bwd, f32_to_16 per step
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": me2e, "steps": args.e2e_steps,
@@ -492,6 +525,7 @@ def run_ours(args, rank, world, local_rank):
         result["layernorm"] = bench_layernorm(dev, pk)
         result["gdp"] = bench_gdp(dev, pk)
     elif not args.skip_extras:
+        result["other_attention_configs"] = bench_other_attention(dev, world=world, rank=rank)
         result.update(bench_ln_gdp_sharded(dev, pk, world))
     return result
 
@@ -558,19 +592,28 @@ def bench_attention_views(dev, packed_ms, steps=10):
             "l2": "flushed between steps (256 MB write, outside the timed events)"}
 
 
-def bench_other_attention(dev, steps=10):
-    """BASELINE's other attention configurations on one GPU, full size: C2 (MSA row attention
-    with pair bias, [512, 8, 256, 32], fwd + the three backward launches) and C5 (triangle
-    attention at N_res = 2048, forward only).  Eager launches, L2 flushed between steps."""
+def bench_other_attention(dev, steps=10, world=1, rank=0):
+    """BASELINE's other attention configurations, full size: C2 (MSA row attention with pair
+    bias, [512, 8, 256, 32], fwd + the three backward launches) and C5 (triangle attention at
+    N_res = 2048, forward only).  With N ranks the attention rows are sharded as in the
+    headline step (every GPU holds the full bias); C2's per-rank dbias partials are summed by an
+    NCCL all-reduce on a side stream that overlaps the accumulator conversion.  Eager launches,
+    L2 flushed between steps (untimed); whole-job TFLOP/s over the slowest rank's mean step."""
     import torch
+    import torch.distributed as dist
     import oracle
     from colabfold_legacy_kernels import torch_ops
+    from colabfold_legacy_kernels.parallel import shard_rows
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    comm = torch.cuda.Stream(dev) if world > 1 else None
 
     def timed(fn):
         for _ in range(3):
             fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         ts = []
         for _ in range(steps):
             flush.zero_()
@@ -580,37 +623,61 @@ def bench_other_attention(dev, steps=10):
             b.record()
             torch.cuda.synchronize()
             ts.append(a.elapsed_time(b))
-        return sorted(ts)[len(ts) // 2]
+        ms = sum(ts) / len(ts)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms
 
     out = {}
     for cfg, backward in ((oracle.configs.C2, True), (oracle.configs.C5, False)):
         t = oracle.configs.make_attention_inputs(cfg, device=dev)
-        q, k, v, bias, kmask, scale = (t[x] for x in ("q", "k", "v", "bias", "kmask", "scale"))
-        n, h, s, d = q.shape
+        n_all, h, s, d = t["q"].shape
+        r0, r1 = shard_rows(n_all, world, rank)
+        q, k, v, kmask = (t[x][r0:r1].contiguous() for x in ("q", "k", "v", "kmask"))
+        bias, scale = t["bias"], t["scale"]
+        dout = t["dout"][r0:r1].contiguous() if backward else None
+        del t
+        n = r1 - r0
         o = torch.empty_like(q)
         lse = torch.empty((n, h, s), dtype=torch.float32, device=dev)
         if backward:
-            dout = t["dout"]
             ws = torch_ops.attention_bwd_workspace(n, h, s, s, d, dev)
             grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
                      torch.empty((h, s, s), dtype=torch.float32, device=dev))
 
             def fn():
+                stream = torch.cuda.current_stream(dev)
                 torch_ops.attention_fwd(q, k, v, bias, kmask, scale, out=o, lse=lse)
-                torch_ops.attention_bwd(q, k, v, bias, kmask, o, lse, dout, scale, workspace=ws,
-                                        grads=grads)
-            flops = attn_flops(n, h, s, d)
+                args = (q, k, v, bias, kmask, o, lse, dout, scale)
+                torch_ops.attention_bwd(*args, workspace=ws, grads=grads, phase=0)
+                torch_ops.attention_bwd(*args, workspace=ws, grads=grads, phase=1)
+                if world > 1:
+                    comm.wait_stream(stream)
+                    with torch.cuda.stream(comm):
+                        dist.all_reduce(grads[3])
+                torch_ops.attention_bwd(*args, workspace=ws, grads=grads, phase=2)
+                if world > 1:
+                    stream.wait_stream(comm)
+            flops = attn_flops(n_all, h, s, d)
         else:
             def fn():
                 torch_ops.attention_fwd(q, k, v, bias, kmask, scale, out=o, lse=lse)
-            flops = 4 * n * h * s * s * d
+            flops = 4 * n_all * h * s * s * d
         ms = timed(fn)
-        out[cfg.name] = {"shape": [n, h, s, d], "pass": "fwd+bwd" if backward else "fwd",
+        out[cfg.name] = {"shape": [n_all, h, s, d], "rows_per_gpu": n,
+                         "pass": "fwd+bwd" if backward else "fwd",
                          "ms": round(ms, 4), "tflops": round(flops / (ms * 1e9), 1),
                          "gflop": round(flops / 1e9, 1)}
-        del t, q, k, v, o, lse, fn
+        if backward and world > 1:
+            out[cfg.name]["dbias_allreduce"] = "NCCL, %d MB f32, side stream beside the convert" \
+                % round(h * s * s * 4 / 1e6, 1)
+        del q, k, v, o, lse, fn
         if backward:
             del ws, grads, dout
+    out["n_gpus"] = world
+    out["scaling"] = "strong (the configuration's rows sharded over the GPUs)"
     out["launch"] = "eager"
     out["l2"] = "flushed between steps (256 MB write, outside the timed events)"
     return out
@@ -683,18 +750,31 @@ def bench_ln_gdp_sharded(dev, pk, world, steps=20):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
-    y, mean, rstd = torch_ops.layer_norm_fwd(x, gamma, beta, 1e-5, return_stats=True)
-    out = torch.empty((m1 - m0, n), dtype=x.dtype, device=dev)
-    ms = {"ln_fwd": slowest(_stream_ms(lambda: torch_ops.layer_norm_fwd(x, gamma, beta, 1e-5,
-                                                                        out=y), steps)),
-          "ln_bwd": slowest(_stream_ms(lambda: sh.layer_norm_bwd(x, gamma, dy, 1e-5, mean, rstd),
-                                       steps)),
-          "gdp_fwd": slowest(_stream_ms(lambda: torch_ops.gdp_fwd(x, wp, bp, wg, bg, mask,
-                                                                  out=out), steps)),
-          "gdp_bwd": slowest(_stream_ms(lambda: sh.gdp_bwd(x, wp, bp, wg, bg, mask, dout),
-                                        steps))}
+    # Consecutive launches rotate over K copies of this rank's shard, K x (x bytes) >= 3 x L2,
+    # so every launch streams its inputs from HBM although one shard may fit in L2 at N >= 4.
+    xbytes = x.numel() * x.element_size()
+    nsets = max(1, min(16, -(-3 * L2_BYTES // xbytes)))
+    sets = [(x, dy, mask, dout)] + [tuple(t.clone() for t in (x, dy, mask, dout))
+                                    for _ in range(nsets - 1)]
+    stats = [torch_ops.layer_norm_fwd(st[0], gamma, beta, 1e-5, return_stats=True) for st in sets]
+    outs = [torch.empty((m1 - m0, n), dtype=x.dtype, device=dev) for _ in sets]
+    ms = {"ln_fwd": slowest(_stream_ms_sets(
+              [lambda i=i: torch_ops.layer_norm_fwd(sets[i][0], gamma, beta, 1e-5,
+                                                    out=stats[i][0]) for i in range(nsets)],
+              steps)),
+          "ln_bwd": slowest(_stream_ms_sets(
+              [lambda i=i: sh.layer_norm_bwd(sets[i][0], gamma, sets[i][1], 1e-5, stats[i][1],
+                                             stats[i][2]) for i in range(nsets)], steps)),
+          "gdp_fwd": slowest(_stream_ms_sets(
+              [lambda i=i: torch_ops.gdp_fwd(sets[i][0], wp, bp, wg, bg, sets[i][2],
+                                             out=outs[i]) for i in range(nsets)], steps)),
+          "gdp_bwd": slowest(_stream_ms_sets(
+              [lambda i=i: sh.gdp_bwd(sets[i][0], wp, bp, wg, bg, sets[i][2], sets[i][3])
+               for i in range(nsets)], steps))}
     note = ("rows sharded over %d GPUs; backward parameter gradients all-reduced once (NCCL); "
-            "inputs larger than L2, launches back to back" % world)
+            "launches back to back rotating over %d copies of the %d MB per-GPU x shard (and its "
+            "dy/dout/mask), %d MB >= 3 x L2, so inputs stream from HBM"
+            % (world, nsets, xbytes >> 20, (nsets * xbytes) >> 20))
 
     def gbs(nbytes, t):
         return nbytes / (t * 1e-3) / 1e9
@@ -721,6 +801,23 @@ def bench_ln_gdp_sharded(dev, pk, world, steps=20):
 
 
 L2_NOTE = "inputs larger than L2 (x 268 MB), launches back to back, no flush"
+L2_BYTES = 126 * 1000 * 1000
+
+
+def _stream_ms_sets(fns, steps):
+    """Mean device time per call of `steps` calls enqueued back to back between two events,
+    call i running fns[i % len(fns)] (each on its own copy of the inputs)."""
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(max(3, len(fns))):
+        fns[i % len(fns)]()
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(steps):
+        fns[i % len(fns)]()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
 
 
 def _stream_ms(fn, steps):
@@ -840,8 +937,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--e2e-steps", type=int, default=8)
-    ap.add_argument("--cpu-rows", type=int, default=32,
-                    help="attention rows in one CPU sample (reference arm and cpu_baseline)")
+    ap.add_argument("--ref-rows", type=int, default=0,
+                    help="reference arm: attention rows per step (default: all 768)")
     ap.add_argument("--skip-extras", action="store_true", help="skip LayerNorm/GDP lines")
     ap.add_argument("--no-graph", action="store_true",
                     help="time the eager step only (no CUDA-graph replay)")

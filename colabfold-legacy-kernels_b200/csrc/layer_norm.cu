@@ -10,6 +10,7 @@
 // statistics need only log2(LPR) shuffles.  Each warp keeps U row groups in flight to cover
 // DRAM latency.  Any other C takes a warp-per-row path with scalar accesses.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -696,24 +697,35 @@ constexpr size_t kNoAllocFloats = static_cast<size_t>(kNoAllocMaxParts) * 2 * kN
 static __device__ __align__(256) float g_ln_noalloc_scratch[kNoAllocFloats];
 
 constexpr int kMaxDev = 64;
-std::once_flag g_noalloc_once[kMaxDev];
-float* g_noalloc_ptr[kMaxDev];
-cudaError_t g_noalloc_err[kMaxDev];
+std::atomic<float*> g_noalloc_ptr[kMaxDev];
+std::mutex g_noalloc_mu;
 
 // Device address of the scratch on the current device.  The array's name is only a host-side
-// stand-in, so the address comes from cudaGetSymbolAddress, once per device, with that device
-// current.
+// stand-in, so the address comes from cudaGetSymbolAddress, with that device current.  Only a
+// successful lookup is kept: a lookup that failed (for example a first call made while a
+// stream capture was open) is retried by the next call.
 int noalloc_scratch(int dev, float** out) {
-    std::call_once(g_noalloc_once[dev], [dev]() {
-        void* p = nullptr;
-        g_noalloc_err[dev] = cudaGetSymbolAddress(&p, g_ln_noalloc_scratch);
-        g_noalloc_ptr[dev] = static_cast<float*>(p);
-    });
-    if (g_noalloc_err[dev] != cudaSuccess || !g_noalloc_ptr[dev]) {
-        return fail(CFK_ERR_LAUNCH, "cfk_ln_bwd_noalloc: cudaGetSymbolAddress failed: %s",
-                    cudaGetErrorString(g_noalloc_err[dev]));
+    if (dev < 0 || dev >= kMaxDev) {
+        return fail(CFK_ERR_INVALID_ARGUMENT,
+                    "cfk_ln_bwd_noalloc: device ordinal %d outside the %d devices it serves", dev,
+                    kMaxDev);
     }
-    *out = g_noalloc_ptr[dev];
+    float* p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+    if (!p) {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        p = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+        if (!p) {
+            void* addr = nullptr;
+            const cudaError_t err = cudaGetSymbolAddress(&addr, g_ln_noalloc_scratch);
+            if (err != cudaSuccess || !addr) {
+                return fail(CFK_ERR_LAUNCH, "cfk_ln_bwd_noalloc: cudaGetSymbolAddress failed: %s",
+                            cudaGetErrorString(err));
+            }
+            p = static_cast<float*>(addr);
+            g_noalloc_ptr[dev].store(p, std::memory_order_release);
+        }
+    }
+    *out = p;
     return CFK_OK;
 }
 

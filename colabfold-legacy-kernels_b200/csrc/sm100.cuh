@@ -25,7 +25,14 @@ enum : uint32_t {
 // One word per process and device; read through cfk_device_status().
 extern __device__ uint32_t g_status_word;
 
-constexpr unsigned long long kWaitLimitNs = 1000000000ull; // about one second
+// How long a wait may take before it gives up, per device (cfk_set_wait_limit_ns); one second
+// unless changed.
+constexpr unsigned long long kDefaultWaitLimitNs = 1000000000ull;
+extern __device__ unsigned long long g_wait_limit_ns;
+
+__device__ __forceinline__ unsigned long long wait_limit_ns() {
+    return *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+}
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -72,14 +79,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete.  Gives up after kWaitLimitNs, or as
-// soon as another thread of the CTA has given up (*abort != 0).  Returns false on giving up.
+// Waits for the phase with the given parity to complete.  Gives up after the device's wait
+// limit (wait_limit_ns()), or as soon as another thread of the CTA has given up
+// (*abort != 0).  Returns false on giving up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile uint32_t* abort) {
     if (mbar_try_wait(bar, parity)) {
         return true;
     }
     const unsigned long long t0 = global_ns();
+    const unsigned long long limit = wait_limit_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) {
             return true;
@@ -87,7 +96,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
         if (*abort) {
             return false;
         }
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit) {
             *abort = 1;
             atomicOr(&g_status_word, kStatusTimeoutBarrier);
             return false;
@@ -125,8 +134,11 @@ __device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
     return v;
 }
 
-static __device__ __noinline__ bool mbar_wait_slow_s(uint32_t bar, uint32_t parity,
-                                                     uint32_t abort) {
+// The waiting loop with an explicit limit (ns): gives up when the limit has passed or the
+// CTA's abort word (shared-memory address) is set; giving up sets the abort word and records
+// kStatusTimeoutBarrier in the status word.
+static __device__ __noinline__ bool mbar_wait_limit_s(uint32_t bar, uint32_t parity,
+                                                      uint32_t abort, unsigned long long limit) {
     const unsigned long long t0 = global_ns();
     while (true) {
         if (mbar_try_wait_s(bar, parity)) {
@@ -135,12 +147,17 @@ static __device__ __noinline__ bool mbar_wait_slow_s(uint32_t bar, uint32_t pari
         if (ld_shared_u32(abort)) {
             return false;
         }
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit) {
             asm volatile("st.shared.u32 [%0], 1;" ::"r"(abort) : "memory");
             atomicOr(&g_status_word, kStatusTimeoutBarrier);
             return false;
         }
     }
+}
+
+static __device__ __noinline__ bool mbar_wait_slow_s(uint32_t bar, uint32_t parity,
+                                                     uint32_t abort) {
+    return mbar_wait_limit_s(bar, parity, abort, wait_limit_ns());
 }
 
 // Waits for the phase with the given parity; gives up like mbar_wait (abort = address of the

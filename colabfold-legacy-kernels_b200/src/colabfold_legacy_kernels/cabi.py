@@ -87,6 +87,9 @@ SIGNATURES = {
                     _vp, _sz, _i64, _i64, _i64],
     "cfk_device_status": [ctypes.POINTER(ctypes.c_uint32)],
     "cfk_clear_device_status": [],
+    "cfk_set_wait_limit_ns": [ctypes.c_uint64],
+    "cfk_get_wait_limit_ns": [ctypes.POINTER(ctypes.c_uint64)],
+    "cfk_test_wait_timeout": [_vp, ctypes.c_uint64, _vp],
 }
 
 _lib = None
@@ -149,3 +152,14 @@ def device_status():
 
 def clear_device_status():
     call("cfk_clear_device_status")
+
+
+def set_wait_limit_ns(ns):
+    """Wait limit of the current device's kernels (cfk_set_wait_limit_ns)."""
+    call("cfk_set_wait_limit_ns", int(ns))
+
+
+def get_wait_limit_ns():
+    out = ctypes.c_uint64(0)
+    call("cfk_get_wait_limit_ns", ctypes.byref(out))
+    return int(out.value)

@@ -5,9 +5,33 @@ device raises.
 These exist for tests, benchmarks and PyTorch users; XLA users go through the FFI handlers.
 """
 
+import os
+
 import torch
 
 from . import cabi
+
+# Opt-in checking of the device status word after every call (CFK_CHECK_STATUS=1): each call
+# then synchronises its device and raises CfkError if a kernel wait gave up, whose outputs are
+# undefined.  Off by default, since the synchronisation serialises the host with the GPU.
+CHECK_STATUS = os.environ.get("CFK_CHECK_STATUS", "") not in ("", "0")
+
+
+def check_status(device=None):
+    """Synchronises `device` and raises CfkError if a kernel wait on it gave up since the
+    status word was last cleared (cabi.clear_device_status)."""
+    with torch.cuda.device(device):
+        torch.cuda.synchronize()
+        code = cabi.device_status()
+    if code:
+        raise cabi.CfkError("cfk_device_status", cabi.CFK_ERR_LAUNCH,
+                            "a kernel wait gave up (status word %d); outputs since then are "
+                            "undefined" % code)
+
+
+def _done(device):
+    if CHECK_STATUS:
+        check_status(device)
 
 _DTYPES = {torch.float16: cabi.CFK_F16, torch.bfloat16: cabi.CFK_BF16}
 
@@ -76,6 +100,7 @@ def attention_fwd(q, k, v, bias, kmask, scale, return_lse=True, out=None, lse=No
             cabi.call("cfk_attn_fwd", *args)
         else:
             cabi.call("cfk_attn_fwd_strided", *args, views)
+    _done(q.device)
     return (out, lse) if return_lse else out
 
 
@@ -118,6 +143,7 @@ def attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, workspace=None, g
             cabi.call("cfk_attn_bwd_strided", *args, views)
         else:
             cabi.call("cfk_attn_bwd_phase_strided", int(phase), *args, views)
+    _done(q.device)
     return dq, dk, dv, dbias
 
 
@@ -132,6 +158,7 @@ def layer_norm_fwd(x, gamma, beta, eps, return_stats=False, out=None):
     with torch.cuda.device(x.device):
         cabi.call("cfk_ln_fwd", _stream(x.device), _dtype_code(x), _ptr(x), _ptr(gamma),
                   _ptr(beta), _ptr(y), _ptr(mean), _ptr(rstd), m, c, float(eps))
+    _done(x.device)
     return (y, mean, rstd) if return_stats else y
 
 
@@ -157,6 +184,7 @@ def layer_norm_bwd(x, gamma, dy, eps, mean=None, rstd=None, workspace=None, grad
         cabi.call("cfk_ln_bwd", _stream(x.device), _dtype_code(x), _ptr(x), _ptr(gamma),
                   _ptr(mean), _ptr(rstd), _ptr(dy), _ptr(dx), _ptr(dgamma), _ptr(dbeta),
                   _ptr(workspace), workspace.numel(), m, c, float(eps))
+    _done(x.device)
     return dx, dgamma, dbeta
 
 
@@ -170,6 +198,7 @@ def gdp_fwd(x, wp, bp, wg, bg, mask, out=None):
     with torch.cuda.device(x.device):
         cabi.call("cfk_gdp_fwd", _stream(x.device), _dtype_code(x), _ptr(x), _ptr(wp), _ptr(bp),
                   _ptr(wg), _ptr(bg), _ptr(mask), _ptr(out), m, k, n)
+    _done(x.device)
     return out
 
 
@@ -193,6 +222,7 @@ def ln_gdp_fwd(z, gamma, beta, eps, wp, bp, wg, bg, mask, out=None, return_stats
         cabi.call("cfk_ln_gdp_fwd", _stream(z.device), _dtype_code(z), _ptr(z), _ptr(gamma),
                   _ptr(beta), float(eps), _ptr(wp), _ptr(bp), _ptr(wg), _ptr(bg), _ptr(mask),
                   _ptr(out), _ptr(mean), _ptr(rstd), _ptr(workspace), workspace.numel(), m, k, n)
+    _done(z.device)
     return (out, mean, rstd) if return_stats else out
 
 
@@ -222,6 +252,7 @@ def gdp_bwd(x, wp, bp, wg, bg, mask, dout, workspace=None, grads=None):
         cabi.call("cfk_gdp_bwd", _stream(x.device), _dtype_code(x), _ptr(x), _ptr(wp), _ptr(bp),
                   _ptr(wg), _ptr(bg), _ptr(mask), _ptr(dout), _ptr(dx), _ptr(dwp), _ptr(dbp),
                   _ptr(dwg), _ptr(dbg), _ptr(workspace), workspace.numel(), m, k, n)
+    _done(x.device)
     return dx, dwp, dbp, dwg, dbg
 
 
@@ -234,6 +265,7 @@ def gate_fwd(g, o, out=None):
     with torch.cuda.device(g.device):
         cabi.call("cfk_gate_fwd", _stream(g.device), _dtype_code(g), _ptr(g), _ptr(o), _ptr(y),
                   g.numel())
+    _done(g.device)
     return y
 
 
@@ -246,4 +278,5 @@ def gate_bwd(g, o, dy):
     with torch.cuda.device(g.device):
         cabi.call("cfk_gate_bwd", _stream(g.device), _dtype_code(g), _ptr(g), _ptr(o), _ptr(dy),
                   _ptr(d_o), _ptr(dg), g.numel())
+    _done(g.device)
     return d_o, dg

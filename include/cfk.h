@@ -169,7 +169,8 @@ CFK_API int cfk_ln_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, cons
  * in a static device array of 2.5 MiB (held by every GPU that loads the library until the
  * process exits), so C must be <= 1024 (larger C is rejected with CFK_ERR_INVALID_ARGUMENT).
  * The first call on a device looks up the array's device address with that device current;
- * make that first call before any stream capture.  All calls share the array: each launch
+ * make that first call before any stream capture (a lookup that fails is not cached: the next
+ * call retries it).  Device ordinals 0-63 are served.  All calls share the array: each launch
  * rewrites the partials it reads, so nothing carries over, but calls that overlap on the GPU
  * (for example on two streams of one device) race.  Results equal cfk_ln_bwd's up to the
  * summation order of dgamma and dbeta. */
@@ -216,12 +217,30 @@ CFK_API int cfk_gdp_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, con
 /* ------------------------------------------------------------------------------------------ */
 
 /* Every wait inside a kernel (on a barrier or on the tensor-memory pipeline) gives up after
- * about one second.  It then records a code in a per-device status word and the kernel returns
- * early instead of hanging.  This reads the word of the current device (0 = no timeout seen). */
+ * the device's wait limit (one second unless cfk_set_wait_limit_ns changed it).  It then
+ * records a code in a per-device status word and the kernel returns early instead of hanging;
+ * the outputs of every launch that ran while the word was set are undefined.  This reads the
+ * word of the current device (0 = no timeout seen; 1 = a barrier wait ran past its limit). */
 CFK_API int cfk_device_status(uint32_t* code);
 
 /* Clears the status word of the current device. */
 CFK_API int cfk_clear_device_status(void);
+
+/* Sets the wait limit of the current device in nanoseconds, in [1e5, 6e11] (0.1 ms to ten
+ * minutes); launches enqueued afterwards use it.  A shared GPU that time-slices between
+ * processes can stretch a healthy wait, so a caller that shares its GPU may raise the limit.
+ * Synchronous (a copy into device memory); call it outside stream capture. */
+CFK_API int cfk_set_wait_limit_ns(uint64_t ns);
+
+/* Reads the wait limit of the current device. */
+CFK_API int cfk_get_wait_limit_ns(uint64_t* ns);
+
+/* Self-test of the give-up path: launches one warp that waits on a barrier no thread arrives
+ * on, through the kernels' own waiting loop, with a limit of limit_ns (in [1e5, 1e8]; 0 = the
+ * device's limit).  The wait gives up, records 1 in the status word and the kernel returns;
+ * *result (device memory, 4 bytes) is set to 1.  No TMA or tensor-core work is in flight, so
+ * the context stays usable.  Clear the status word before the next real launch. */
+CFK_API int cfk_test_wait_timeout(cfk_stream_t stream, uint64_t limit_ns, uint32_t* result);
 
 #ifdef __cplusplus
 } /* extern "C" */

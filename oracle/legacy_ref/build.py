@@ -28,7 +28,24 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 OUT = REPO / "oracle" / "_ref"
-REFERENCE = Path(os.environ.get("CFK_REFERENCE", "/root/reference"))
+
+
+def reference_dir():
+    """The reference checkout: $CFK_REFERENCE, else the `reference_path` that BASELINE.json at
+    the repository root names; None when neither is set or the directory is absent."""
+    path = os.environ.get("CFK_REFERENCE")
+    if not path:
+        try:
+            import json
+            path = json.loads((REPO / "BASELINE.json").read_text()).get("reference_path")
+        except (OSError, ValueError):
+            path = None
+    if path and Path(path).is_dir():
+        return Path(path)
+    return None
+
+
+REFERENCE = reference_dir()
 
 # wrapper -> reference source it includes
 UNITS = {
@@ -66,10 +83,11 @@ def nvcc():
 
 def build(force=False, verbose=True):
     """Builds the libraries when the reference checkout is present; returns their paths."""
-    cuda_dir = REFERENCE / "cuda"
-    if not cuda_dir.is_dir():
+    cuda_dir = REFERENCE / "cuda" if REFERENCE is not None else None
+    if cuda_dir is None or not cuda_dir.is_dir():
         if verbose:
-            print("legacy_ref: no reference checkout at %s; skipped" % REFERENCE)
+            print("legacy_ref: no reference checkout ($CFK_REFERENCE or BASELINE.json "
+                  "reference_path); skipped")
         return []
     OUT.mkdir(parents=True, exist_ok=True)
     inc = cutlass_include()

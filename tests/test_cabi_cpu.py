@@ -167,3 +167,27 @@ def test_gate_arguments_without_device(libpath):
         cabi.call("cfk_gate_bwd", None, cabi.CFK_BF16, 16, 32, 48, 64, 72 + 2, 8)
     assert "aligned" in e.value.message
     assert cabi.call("cfk_gate_fwd", None, cabi.CFK_BF16, None, None, None, 0) == 0
+
+
+def test_wait_limit_and_selftest_arguments_without_device(libpath):
+    """cfk_set_wait_limit_ns and cfk_test_wait_timeout check their arguments before they touch
+    a device."""
+    from colabfold_legacy_kernels import cabi
+    for bad in (0, 10, 99_999, 600_000_000_001):
+        with pytest.raises(cabi.CfkError) as e:
+            cabi.set_wait_limit_ns(bad)
+        assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT and "outside" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_test_wait_timeout", None, 5_000_000, None)
+    assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT and "null" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_test_wait_timeout", None, 10 ** 9, ctypes.c_void_p(16))
+    assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT
+
+
+def test_noalloc_checks_its_width_before_the_device(libpath):
+    from colabfold_legacy_kernels import cabi
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_ln_bwd_noalloc", None, cabi.CFK_BF16, None, None, None, None, None, None,
+                  None, None, 4, 2048, 1e-5)
+    assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT and "1024" in e.value.message

@@ -2,7 +2,8 @@
 
 Attention (ShardedAttention: dbias all-reduced on a side stream) and LayerNorm / GDP
 (ShardedLnGdp: one all-reduce of the flat parameter-gradient buffer), each rank on its own GPU,
-against the same kernels run on the full batch on one GPU.  Row-local outputs computed
+against the same kernels run on the full batch on one GPU, and against the CPU oracle
+(float64; the all-reduced dbias over both ranks' rows).  Row-local outputs computed
 without reductions across CTAs match exactly (a row's result does not depend on the other
 rows); dq/dv to their last bit, and the reduced gradients to f32 summation-order rounding.  NVLS is off (NCCL_NVLS_ENABLE=0) as for every multi-rank test here.
 """
@@ -26,6 +27,19 @@ def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
+
+
+def _excess_bf16(a, e, rtol=2e-2, atol=2e-2):
+    """max(|a - e| - (atol + rtol |e|)) over the elements: <= 0 when every element is within the
+    16-bit tolerance."""
+    a, e = a.double().cpu(), e.double().cpu()
+    return float(((a - e).abs() - (atol + rtol * e.abs())).max())
+
+
+def _excess_f32(a, e, rel=1e-4):
+    """max(|a - e| - rel (|e| + max|e|)): <= 0 when every element is within the f32 tolerance."""
+    a, e = a.double().cpu(), e.double().cpu()
+    return float(((a - e).abs() - rel * (e.abs() + e.abs().max())).max())
 
 
 def _worker(rank, world, port, queue):
@@ -62,6 +76,18 @@ def _worker(rank, world, port, queue):
         errs["attn_dv_bf"] = float((res.dv.float() - dv[r0:r1].float()).abs().max()
                                    / dv.float().abs().max())
         errs["attn_dbias_rel"] = float((res.dbias - db).abs().max() / db.abs().max())
+        # the sharded results against the CPU oracle (float64): this rank's rows, and dbias
+        # summed over both ranks' rows by the all-reduce
+        c = {x: t[x].cpu() for x in ("q", "k", "v", "bias", "kmask", "dout")}
+        r_out, r_lse = oracle.attention_fwd(c["q"], c["k"], c["v"], c["bias"], c["kmask"],
+                                            t["scale"])
+        r = oracle.attention_bwd(c["q"], c["k"], c["v"], c["bias"], c["kmask"], out.cpu(),
+                                 lse.cpu(), c["dout"], t["scale"])
+        errs["oracle_out_excess"] = _excess_bf16(res.out, r_out[r0:r1])
+        errs["oracle_dq_excess"] = _excess_bf16(res.dq, r[0][r0:r1])
+        errs["oracle_dk_excess"] = _excess_bf16(res.dk, r[1][r0:r1])
+        errs["oracle_dv_excess"] = _excess_bf16(res.dv, r[2][r0:r1])
+        errs["oracle_dbias_excess"] = _excess_f32(res.dbias, r[3])
         # LayerNorm + GDP, config C4's shape class at 3000 rows
         ci = oracle.configs.make_ln_gdp_inputs(oracle.configs.LnGdpConfig("c4_small", 3000, 128,
                                                                           256, 3), device=dev)
@@ -105,4 +131,5 @@ def test_two_gpu_sharding_matches_one_gpu():
         assert status == "ok", errs
         for name, err in errs.items():
             bound = 1e-5 if name.endswith("_rel") else (1e-2 if name.endswith("_bf") else 0.0)
+            # *_excess: the oracle tolerance minus the error, <= 0 when within tolerance
             assert err <= bound, (rank, name, err)

@@ -10,11 +10,10 @@ Tolerances as in the other tests: dx (16-bit) rtol = atol = 2e-2; dgamma, dbeta 
 max|.| plus 1e-4 relative.
 """
 
-import ctypes
-
 import pytest
 import torch
 
+import oracle
 from conftest import assert_close_bf16, assert_close_f32
 
 pytestmark = pytest.mark.gpu
@@ -34,7 +33,9 @@ def _noalloc(x, gamma, dy, eps, mean=None, rstd=None):
     return dx, dgamma, dbeta
 
 
-@pytest.mark.parametrize("c,dtype", [(128, torch.bfloat16), (1000, torch.float16)])
+# C = 1024 with 70k rows fills the static scratch exactly (320 partials x 2 x 1024 floats)
+@pytest.mark.parametrize("c,dtype", [(128, torch.bfloat16), (1000, torch.float16),
+                                     (1024, torch.bfloat16)])
 def test_noalloc_matches_workspace_entry_point(cuda_device, c, dtype):
     from colabfold_legacy_kernels import torch_ops
     g = torch.Generator().manual_seed(c)
@@ -53,6 +54,26 @@ def test_noalloc_matches_workspace_entry_point(cuda_device, c, dtype):
         assert_close_bf16(got[0], ref[0], "dx (call %d)" % call)
         assert_close_f32(got[1], ref[1], "dgamma (call %d)" % call)
         assert_close_f32(got[2], ref[2], "dbeta (call %d)" % call)
+        if call == 0:
+            # and against the CPU oracle (float64) on the same 16-bit inputs
+            rdx, rdg, rdb = oracle.layer_norm_bwd(x.cpu(), gamma.cpu(), dy.cpu(), eps)
+            assert_close_bf16(got[0], rdx, "dx vs oracle")
+            assert_close_f32(got[1], rdg, "dgamma vs oracle")
+            assert_close_f32(got[2], rdb, "dbeta vs oracle")
+
+
+def test_noalloc_empty_rows_give_zero_parameter_gradients(cuda_device):
+    """M = 0: no row kernel runs; dgamma and dbeta are written as zeros (after a call that left
+    nonzero partials in the shared array)."""
+    c = 256
+    x = torch.randn(5000, c, device="cuda").to(torch.bfloat16)
+    gamma = torch.ones(c, device="cuda")
+    _noalloc(x, gamma, x, 1e-5)
+    empty = torch.empty(0, c, dtype=torch.bfloat16, device="cuda")
+    dx, dg, db = _noalloc(empty, gamma, empty, 1e-5)
+    torch.cuda.synchronize()
+    assert dx.shape == (0, c)
+    assert dg.abs().sum().item() == 0 and db.abs().sum().item() == 0
 
 
 def test_noalloc_rejects_rows_wider_than_its_scratch(cuda_device):
