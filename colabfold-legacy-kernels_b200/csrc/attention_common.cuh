@@ -72,6 +72,12 @@ __device__ __forceinline__ uint4 lds128(uint32_t saddr) {
     return r;
 }
 
+__device__ __forceinline__ uint2 lds64(uint32_t saddr) {
+    uint2 r;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(saddr));
+    return r;
+}
+
 __device__ __forceinline__ void sts128(uint32_t saddr, uint4 v) {
     asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(saddr), "r"(v.x), "r"(v.y),
                  "r"(v.z), "r"(v.w)
@@ -155,14 +161,15 @@ inline int d8_log2(int d) {
     return d == 8 ? 0 : d == 16 ? 1 : d == 32 ? 2 : 3;
 }
 
-// dst_t = (16-bit) src_t for up to three tensors t in one launch, or zeros where src_t is NULL:
-// src_t packed f32 [N, H, S_t, D] (n8[t] groups of 8 elements), dst_t written through its view.
-// 8 elements per thread and step; D = 8 << d8_log2.
+// dst_t = (16-bit) (mul_t * src_t) for up to three tensors t in one launch, or zeros where src_t
+// is NULL: src_t packed f32 [N, H, S_t, D] (n8[t] groups of 8 elements), dst_t written through
+// its view.  8 elements per thread and step; D = 8 << d8_log2.
 struct ConvertJob {
     const float* src[3];
     void* dst[3];
     int64_t n8[3];
     RowStrides view[3];
+    float mul[3];
     int d8_log2;
 };
 
@@ -185,10 +192,11 @@ __global__ void f32_to_16_kernel(const ConvertJob job) {
         }
         uint4 val = make_uint4(0u, 0u, 0u, 0u);
         if (job.src[t]) {
+            const float m = job.mul[t];
             const float4 a = *reinterpret_cast<const float4*>(job.src[t] + k * 8);
             const float4 b = *reinterpret_cast<const float4*>(job.src[t] + k * 8 + 4);
-            val = make_uint4(E::pack(a.x, a.y), E::pack(a.z, a.w), E::pack(b.x, b.y),
-                             E::pack(b.z, b.w));
+            val = make_uint4(E::pack(a.x * m, a.y * m), E::pack(a.z * m, a.w * m),
+                             E::pack(b.x * m, b.y * m), E::pack(b.z * m, b.w * m));
         }
         const int64_t r = k >> job.d8_log2;
         const int c = static_cast<int>(k & ((1 << job.d8_log2) - 1));

@@ -409,8 +409,8 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
                 if (leader) {
                     bulk_wait_read<0>(); // the previous store has read the staging box
                 }
-                named_bar_sync(1 + w, 128); // every thread arrives, also after a failed wait
-                if (!ok || *abort_flag) {
+                // every thread arrives, also after a failed wait, and all take one decision
+                if (!named_bar_and(1 + w, 128, ok && !*abort_flag)) {
                     goto done;
                 }
                 __syncwarp();
@@ -1526,6 +1526,7 @@ __global__ void __launch_bounds__(DwWarps<EQ>::kThreads, 1)
             accp[j] = make_float2(0.f, 0.f);
             accg[j] = make_float2(0.f, 0.f);
         }
+        bool failed = false; // a wait gave up: leave together at the barrier after the loop
         for (int i = 0; i < n_mine; ++i) {
             const int mt = group + i * n_groups;
             const int row = mt * 128 + r;
@@ -1533,7 +1534,8 @@ __global__ void __launch_bounds__(DwWarps<EQ>::kThreads, 1)
             const float mk = row_ok ? E::to_float(mask[row]) : 0.f;
             if (!mbar_wait(&rec_full[i & 1], (i >> 1) & 1, abort_flag) ||
                 !mbar_wait(&in_full[i & 1], (i >> 1) & 1, abort_flag)) {
-                goto done;
+                failed = true;
+                break;
             }
             __syncwarp();
             tc_fence_after();
@@ -1566,7 +1568,8 @@ __global__ void __launch_bounds__(DwWarps<EQ>::kThreads, 1)
             // hi / lo tiles are free once the dw MMAs of tile i-1 are done (the gate gradients
             // above overlap them)
             if (i > 0 && !mbar_wait(dw_done, (i - 1) & 1, abort_flag)) {
-                goto done;
+                failed = true;
+                break;
             }
             // hi + lo split (16-bit each) into the four MMA operand tiles
             const uint32_t rowoff = r * 128;
@@ -1613,7 +1616,9 @@ __global__ void __launch_bounds__(DwWarps<EQ>::kThreads, 1)
                 red[warp * 2 * CW + CW + lane] = sg;
             }
         }
-        named_bar_sync(1, WR::kEpi * 32);
+        if (!named_bar_and(1, WR::kEpi * 32, !failed && !*abort_flag)) {
+            goto done;
+        }
         if (threadIdx.x < 64) {
             const int ww = threadIdx.x / CW, col = threadIdx.x % CW;
             float sp = 0.f, sg = 0.f;

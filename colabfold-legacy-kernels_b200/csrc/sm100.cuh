@@ -514,4 +514,18 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also returns the AND of `v` over the participating threads: every thread
+// gets the same answer, so a group can decide together whether to go on.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t count, bool v) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\t"
+                 "setp.ne.u32 p, %1, 0;\n\t"
+                 "bar.red.and.pred q, %2, %3, p;\n\t"
+                 "selp.u32 %0, 1, 0, q;\n\t}"
+                 : "=r"(r)
+                 : "r"(v ? 1u : 0u), "r"(id), "r"(count)
+                 : "memory");
+    return r != 0;
+}
+
 } // namespace cfk
