@@ -30,15 +30,18 @@ LIB = OUT_DIR / "libcfk_sm100.so"
 XLA_LIB = OUT_DIR / "libcfk_xla_sm100.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+# No relocatable device code: ptxas ignores setmaxnreg in relocatable code, so the kernels are
+# compiled as one translation unit (csrc/all_kernels.cu includes every kernel source).
 NVCC_FLAGS = [
-    "-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC",
+    "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
     "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
     "-diag-suppress", "177,550",
 ] + ARCH
 
-# The kernels and the C ABI.  ffi_handlers.cc is built separately (needs the XLA headers).
-SOURCES = ["host.cpp", "status.cu", "layer_norm.cu", "attention_fwd.cu", "attention_bwd.cu",
-           "gdp.cu", "gate.cu"]
+# The kernels (one unit including status.cu, layer_norm.cu, attention_fwd.cu, attention_bwd.cu,
+# gdp.cu and gate.cu) and the host helpers.  ffi_handlers.cc is built separately (needs the XLA
+# headers).
+SOURCES = ["host.cpp", "all_kernels.cu"]
 
 
 def nvcc():
@@ -49,7 +52,9 @@ def nvcc():
 
 
 def headers():
-    return list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
+    # every kernel source is an include of all_kernels.cu, so each is a dependency of it
+    return (list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h")) +
+            [p for p in CSRC.glob("*.cu") if p.name != "all_kernels.cu"])
 
 
 def stale(target, deps):
@@ -73,7 +78,7 @@ def compile_one(src, extra, force):
 
 
 def link(objs, out, extra_libs=()):
-    cmd = [nvcc()] + ARCH + ["-shared", "-rdc=true", "-cudart", "static",
+    cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static",
                              "-Xcompiler", "-static-libstdc++", "-Xcompiler", "-static-libgcc",
                              "-Xlinker", "--exclude-libs,ALL", "-o", str(out)] + [str(o) for o in objs] + list(extra_libs)
     r = subprocess.run(cmd, capture_output=True, text=True)

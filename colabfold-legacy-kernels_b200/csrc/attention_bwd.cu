@@ -48,6 +48,7 @@
 // Head dim 64 (attn_bwd_inplace_kernel) keeps the first design: its partial-sum buffers need the
 // tensor-memory columns, so P^T and dS^T overwrite S^T and dP^T, the row statistics come from
 // shared memory per score, and the dS warps drain the partials themselves.
+#include <cstdlib>
 #include <type_traits>
 
 #include "attention_common.cuh"
@@ -63,6 +64,8 @@ struct BwdParams {
     const uint8_t* stats;  // kStatBytes per (batch row, head, query tile)
     float* dbias_out;      // dbias, or the first batch chunk's partial tile set
     int64_t dbias_stride;  // floats between the partials of consecutive batch chunks (0: one)
+    int dbias_accumulate;  // add this launch's sums to dbias_out (rows of earlier launches)
+    int b_base, b_end;     // the batch rows of this launch (the accumulators hold b - b_base)
     int N, H, Sq, Sk;
     int n_it, n_jt, n_bc, bchunk;
     int64_t items;
@@ -289,7 +292,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         for (int it = 0; it < n_items_mine; ++it) {
             const BwdItem w = decode_item(p, blockIdx.x + static_cast<int64_t>(it) * gridDim.x);
             const int i0 = w.itile * kBM, j0 = w.jt * kBN;
-            const int b_lo = w.bc * p.bchunk, b_hi = min(p.N, b_lo + p.bchunk);
+            const int b_lo = p.b_base + w.bc * p.bchunk, b_hi = min(p.b_end, b_lo + p.bchunk);
             bool ok = true;
             for (int b = b_lo; b < b_hi; ++b, ++g) {
                 const int s = g % NST;
@@ -343,7 +346,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         int total_steps = 0;
         for (int it = 0; it < n_items_mine; ++it) {
             const BwdItem w = decode_item(p, blockIdx.x + static_cast<int64_t>(it) * gridDim.x);
-            const int b_lo = w.bc * p.bchunk, b_hi = min(p.N, b_lo + p.bchunk);
+            const int b_lo = p.b_base + w.bc * p.bchunk, b_hi = min(p.b_end, b_lo + p.bchunk);
             total_steps += max(0, b_hi - b_lo);
         }
         // dV = P^T dO, dK = dS^T Q (A in tensor memory), dQ = dS K (A = dS^T rows in shared
@@ -427,7 +430,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         for (int it = 0; it < n_items_mine; ++it) {
             const BwdItem w = decode_item(p, blockIdx.x + static_cast<int64_t>(it) * gridDim.x);
             const int i0 = w.itile * kBM, j0 = w.jt * kBN;
-            const int b_lo = w.bc * p.bchunk, b_hi = min(p.N, b_lo + p.bchunk);
+            const int b_lo = p.b_base + w.bc * p.bchunk, b_hi = min(p.b_end, b_lo + p.bchunk);
             for (int b = b_lo; b < b_hi; ++b, ++g) {
                 const bool ok = mbar_wait(part_full, g & 1, abort_flag);
                 // one decision for the whole warpgroup, or some threads would wait at the next
@@ -437,35 +440,40 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
                 }
                 __syncwarp();
                 tc_fence_after();
-                const int bh = b * p.H + w.h;
-#pragma unroll
+                const int bh = (b - p.b_base) * p.H + w.h; // accumulator rows of this launch
+#pragma unroll 1
                 for (int pp = 0; pp < 3; ++pp) {
-                    uint32_t raw[D];
-#pragma unroll
-                    for (int c0 = 0; c0 < D; c0 += 8) {
-                        tmem_ld8(tmem + lane_off + C::kPartBase + pp * G::kDp + c0,
-                                 *reinterpret_cast<uint32_t (*)[8]>(&raw[c0]));
-                    }
-                    tmem_ld_wait();
-                    if (pp == 2) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) {
-                            mbar_arrive(part_empty);
-                        }
-                    }
                     const uint32_t stg = sbase + C::kOffStg + (pc & 1) * C::kStgBytes;
                     if (leader) {
                         bulk_wait_read<1>(); // the reduce two partials back has read this buffer
                     }
                     named_bar_sync(1, 128);
+                    // at most 16 columns in registers at a time (this warpgroup runs with few)
+                    constexpr int kHalf = D < 16 ? D : 16;
 #pragma unroll
-                    for (int q = 0; q < D / 4; ++q) {
-                        const int col = q * 4;
-                        sts128(stg + (col / C::kPW) * C::kPanelBytes +
-                                   stg_chunk<C::kRowB>(row, (col % C::kPW) / 4),
-                               make_uint4(raw[4 * q], raw[4 * q + 1], raw[4 * q + 2],
-                                          raw[4 * q + 3]));
+                    for (int h0 = 0; h0 < D; h0 += kHalf) {
+                        uint32_t raw[kHalf];
+#pragma unroll
+                        for (int c0 = 0; c0 < kHalf; c0 += 8) {
+                            tmem_ld8(tmem + lane_off + C::kPartBase + pp * G::kDp + h0 + c0,
+                                     *reinterpret_cast<uint32_t (*)[8]>(&raw[c0]));
+                        }
+                        tmem_ld_wait();
+                        if (pp == 2 && h0 + kHalf == D) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) {
+                                mbar_arrive(part_empty);
+                            }
+                        }
+#pragma unroll
+                        for (int q = 0; q < kHalf / 4; ++q) {
+                            const int col = h0 + q * 4;
+                            sts128(stg + (col / C::kPW) * C::kPanelBytes +
+                                       stg_chunk<C::kRowB>(row, (col % C::kPW) / 4),
+                                   make_uint4(raw[4 * q], raw[4 * q + 1], raw[4 * q + 2],
+                                              raw[4 * q + 3]));
+                        }
                     }
                     fence_proxy_async_smem();
                     named_bar_sync(1, 128);
@@ -505,7 +513,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             const BwdItem wi = decode_item(p, blockIdx.x + static_cast<int64_t>(it) * gridDim.x);
             const int h = wi.h;
             const int i0 = wi.itile * kBM, j0 = wi.jt * kBN;
-            const int b_lo = wi.bc * p.bchunk, b_hi = min(p.N, b_lo + p.bchunk);
+            const int b_lo = p.b_base + wi.bc * p.bchunk, b_hi = min(p.b_end, b_lo + p.bchunk);
             const int j = j0 + jl;
             // bias^T: this thread's key j against queries [i0 + 32w, +32), as 16-bit pairs in
             // its own shared-memory row (read back by this thread only)
@@ -644,7 +652,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
 #pragma unroll
                 for (int t = 0; t < 32; ++t) {
                     if (t < n) {
-                        *o = dbias[t];
+                        *o = p.dbias_accumulate ? *o + dbias[t] : dbias[t];
                     }
                     o += p.Sk;
                 }
@@ -1264,13 +1272,13 @@ __global__ void __launch_bounds__(128)
     }
 }
 
-// dbias = the batch chunks' partial tiles added in chunk order.
+// dbias (+)= the batch chunks' partial tiles added in chunk order.
 __global__ void dbias_chunks_kernel(const float* __restrict__ part, float* __restrict__ dbias,
-                                    int64_t n, int chunks) {
+                                    int64_t n, int chunks, int accumulate) {
     for (int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < n;
          x += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        float acc = part[x];
-        for (int c = 1; c < chunks; ++c) {
+        float acc = accumulate ? dbias[x] : 0.f;
+        for (int c = 0; c < chunks; ++c) {
             acc += part[c * n + x];
         }
         dbias[x] = acc;
@@ -1285,25 +1293,54 @@ constexpr size_t align256(size_t x) {
 // SM count of every compute capability 10.0 part).
 constexpr int kWorkspaceSms = 160;
 
+// f32 accumulator bytes one launch of the main kernel may use; larger problems are processed in
+// ranges of batch rows, one launch each, which bounds the workspace.  (Ranges small enough for
+// the accumulators to stay in the 126 MB L2 were measured slower at tri-768: 3.37 against
+// 2.85 ms per step, the per-launch pipeline fill and drain outweighing the L2-resident
+// reductions.)
+constexpr int64_t kRangeAccBytes = 4ll << 30;
+
 // Batch chunks of a launch with `base` (head, query tile, key tile) items: as many as fit in
-// one wave of `sms` CTAs, at least one, at most N.
-int64_t batch_chunks(int64_t N, int64_t base, int64_t sms) {
-    if (base <= 0 || N <= 0) {
+// one wave of `sms` CTAs, at least one, at most the launch's rows.
+int64_t batch_chunks(int64_t rows, int64_t base, int64_t sms) {
+    if (base <= 0 || rows <= 0) {
         return 1;
     }
     int64_t nbc = base >= sms ? 1 : std::max<int64_t>(1, sms / base);
-    return std::min<int64_t>(nbc, N);
+    return std::min<int64_t>(nbc, rows);
+}
+
+// Batch rows per launch of the main kernel (head dim 64 keeps all rows in one launch).  The
+// accumulator budget can be lowered through $CFK_BWD_RANGE_BYTES (tests use it to exercise
+// several ranges on small problems).
+int64_t range_rows(int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D) {
+    const int64_t row_bytes = 4 * H * (Sq + 2 * Sk) * D;
+    if (D == 64 || row_bytes <= 0) {
+        return std::max<int64_t>(N, 1);
+    }
+    int64_t budget = kRangeAccBytes;
+    if (const char* env = std::getenv("CFK_BWD_RANGE_BYTES")) {
+        const long long v = std::atoll(env);
+        if (v > 0) {
+            budget = v;
+        }
+    }
+    const int64_t r = std::max<int64_t>(1, budget / row_bytes);
+    // one launch when the split would buy little
+    return N <= r + r / 2 ? std::max<int64_t>(N, 1) : r;
 }
 
 struct BwdWorkspace {
     size_t dq_off, dk_off, dv_off, stat_off, dbp_off, total;
-    int64_t max_chunks;
+    int64_t range;       // batch rows per launch of the main kernel
+    int64_t max_chunks;  // batch chunks (dbias partials) of one launch at most
 };
 
 BwdWorkspace bwd_workspace(int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D) {
     BwdWorkspace w;
-    const size_t eq = static_cast<size_t>(N * H * Sq * D) * 4;
-    const size_t ekv = static_cast<size_t>(N * H * Sk * D) * 4;
+    w.range = std::min<int64_t>(range_rows(N, H, Sq, Sk, D), std::max<int64_t>(N, 1));
+    const size_t eq = static_cast<size_t>(w.range * H * Sq * D) * 4;
+    const size_t ekv = static_cast<size_t>(w.range * H * Sk * D) * 4;
     const int64_t n_it = (Sq + kBM - 1) / kBM;
     const int64_t n_jt = (Sk + kBN - 1) / kBN;
     w.dq_off = 0;
@@ -1312,15 +1349,19 @@ BwdWorkspace bwd_workspace(int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t
     w.stat_off = w.dv_off + align256(ekv);
     w.dbp_off = w.stat_off + align256(static_cast<size_t>(N * H * n_it) * kStatBytes);
     // batch rows per chunk -> number of chunks, as the launch computes it
-    const int64_t nbc = batch_chunks(N, H * n_it * n_jt, kWorkspaceSms);
-    const int64_t bchunk = (N + nbc - 1) / std::max<int64_t>(nbc, 1);
-    w.max_chunks = bchunk > 0 ? (N + bchunk - 1) / bchunk : 1;
+    const int64_t nbc = batch_chunks(w.range, H * n_it * n_jt, kWorkspaceSms);
+    const int64_t bchunk = (w.range + nbc - 1) / std::max<int64_t>(nbc, 1);
+    w.max_chunks = bchunk > 0 ? (w.range + bchunk - 1) / bchunk : 1;
     w.total = w.dbp_off + (w.max_chunks > 1 ? align256(static_cast<size_t>(w.max_chunks * H * Sq *
                                                                           Sk) * 4)
                                             : 0);
     return w;
 }
 
+// Phase 0 (bit 1): row statistics of every row.  Phase 1 (bit 2): per range of batch rows,
+// zero the accumulators, run the main kernel and convert the range's dq, dk, dv -- except the
+// last range's conversion, which is phase 2 (bit 4); dbias is final after phase 1, so a
+// caller can reduce it across GPUs while phase 2 runs.
 template <typename T, int D>
 int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                const void* v, const void* bias, const uint8_t* kmask, const void* out,
@@ -1346,70 +1387,92 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
     p.Sk = Sk;
     p.n_it = (Sq + kBM - 1) / kBM;
     p.n_jt = (Sk + kBN - 1) / kBN;
-    const int64_t base = static_cast<int64_t>(H) * p.n_it * p.n_jt;
-    // batch chunks: as many as fit in one wave of CTAs, within what the workspace holds
-    int64_t nbc = std::min(batch_chunks(N, base, dev.num_sms), wl.max_chunks);
-    p.bchunk = static_cast<int>((N + nbc - 1) / nbc);
-    p.n_bc = static_cast<int>((N + p.bchunk - 1) / p.bchunk);
-    p.items = base * p.n_bc;
     p.scale = scale;
     p.mask_bits = mask_bias_bits(scale);
-    const bool chunked = p.n_bc > 1;
-    p.dbias_out = chunked ? reinterpret_cast<float*>(ws + wl.dbp_off) : dbias;
-    p.dbias_stride = chunked ? static_cast<int64_t>(H) * Sq * Sk : 0;
+    const int64_t base = static_cast<int64_t>(H) * p.n_it * p.n_jt;
 
-    const int64_t nh = static_cast<int64_t>(N) * H;
     if (phases & 1) {
-        if (cudaMemsetAsync(ws, 0, wl.stat_off, st) != cudaSuccess) {
-            return fail(CFK_ERR_LAUNCH, "cfk_attn_bwd: memset failed");
-        }
+        const int64_t nh = static_cast<int64_t>(N) * H;
         attn_bwd_prep_kernel<T, D><<<static_cast<unsigned>(nh * p.n_it), 128, 0, st>>>(
             static_cast<const T*>(out), static_cast<const T*>(dout), lse, stats, Sq, p.n_it, scale,
             kInplace ? 0u : p.mask_bits, row_strides(views[3], D), row_strides(views[4], D));
         CFK_TRY(check_launch("attn_bwd_prep"));
     }
+    if (!(phases & 6)) {
+        return CFK_OK;
+    }
+    CUtensorMap tq, tk, tv, tdo;
     if (phases & 2) {
-        CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
         CFK_TRY(make_tmap_rows(&tq, q, views[0], D, kBM, G::kSwizzleBytes, "bwd q"));
         CFK_TRY(make_tmap_rows(&tk, k, views[1], D, kBN, G::kSwizzleBytes, "bwd k"));
         CFK_TRY(make_tmap_rows(&tv, v, views[2], D, kBN, G::kSwizzleBytes, "bwd v"));
         CFK_TRY(make_tmap_rows(&tdo, dout, views[4], D, kBM, G::kSwizzleBytes, "bwd dout"));
-        const uint64_t frow = 4ull * D;
-        CFK_TRY(make_tmap_3d(&tdq, dq_acc, D, Sq, nh, frow, frow * Sq, C::kPW, kBM, 1, C::kRowB,
-                             "bwd dq acc", true));
-        CFK_TRY(make_tmap_3d(&tdk, dk_acc, D, Sk, nh, frow, frow * Sk, C::kPW, kBN, 1, C::kRowB,
-                             "bwd dk acc", true));
-        CFK_TRY(make_tmap_3d(&tdv, dv_acc, D, Sk, nh, frow, frow * Sk, C::kPW, kBN, 1, C::kRowB,
-                             "bwd dv acc", true));
-        auto kern = kInplace ? attn_bwd_inplace_kernel<T, 64> : attn_bwd_kernel<T, (D < 64 ? D : 32)>;
-        CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, C::kSmemBytes,
-                                 "attn_bwd"));
-        const int grid = static_cast<int>(std::min<int64_t>(p.items, dev.num_sms));
-        kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, tdq, tdk, tdv, p);
-        CFK_TRY(check_launch("attn_bwd"));
-        if (chunked) {
-            const int64_t n = static_cast<int64_t>(H) * Sq * Sk;
-            const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, dev.num_sms * 8));
-            dbias_chunks_kernel<<<blocks, 256, 0, st>>>(p.dbias_out, dbias, n, p.n_bc);
-            CFK_TRY(check_launch("attn_bwd dbias chunks"));
-        }
     }
-    if (!(phases & 4)) {
-        return CFK_OK;
-    }
-    const int64_t rows = static_cast<int64_t>(N) * H * Sq;
-    const int64_t kv8 = static_cast<int64_t>(N) * H * Sk * D / 8;
+    const int64_t n_ranges = (N + wl.range - 1) / wl.range;
     // the first design's dS carries the softmax scale; the second's is unscaled
     const float mqk = kInplace ? 1.f : scale;
-    const ConvertJob job{{dq_acc, dk_acc, dv_acc},
-                         {dq, dk, dv},
-                         {rows * D / 8, kv8, kv8},
-                         {row_strides(views[5], D), row_strides(views[6], D),
-                          row_strides(views[7], D)},
-                         {mqk, mqk, 1.f},
-                         d8_log2(D)};
-    f32_to_16_kernel<T><<<dev.num_sms * 8, 256, 0, st>>>(job);
-    return check_launch("attn_bwd convert");
+    for (int64_t rg = 0; rg < n_ranges; ++rg) {
+        const int b0 = static_cast<int>(rg * wl.range);
+        const int nr = static_cast<int>(std::min<int64_t>(wl.range, N - b0));
+        const int64_t nh = static_cast<int64_t>(nr) * H;
+        const bool last = rg + 1 == n_ranges;
+        if (phases & 2) {
+            if (cudaMemsetAsync(ws, 0, wl.stat_off, st) != cudaSuccess) {
+                return fail(CFK_ERR_LAUNCH, "cfk_attn_bwd: memset failed");
+            }
+            CUtensorMap tdq, tdk, tdv;
+            const uint64_t frow = 4ull * D;
+            CFK_TRY(make_tmap_3d(&tdq, dq_acc, D, Sq, nh, frow, frow * Sq, C::kPW, kBM, 1,
+                                 C::kRowB, "bwd dq acc", true));
+            CFK_TRY(make_tmap_3d(&tdk, dk_acc, D, Sk, nh, frow, frow * Sk, C::kPW, kBN, 1,
+                                 C::kRowB, "bwd dk acc", true));
+            CFK_TRY(make_tmap_3d(&tdv, dv_acc, D, Sk, nh, frow, frow * Sk, C::kPW, kBN, 1,
+                                 C::kRowB, "bwd dv acc", true));
+            // batch chunks: as many as fit in one wave of CTAs, within what the workspace holds
+            const int64_t nbc = std::min(batch_chunks(nr, base, dev.num_sms), wl.max_chunks);
+            p.bchunk = static_cast<int>((nr + nbc - 1) / nbc);
+            p.n_bc = static_cast<int>((nr + p.bchunk - 1) / p.bchunk);
+            p.items = base * p.n_bc;
+            p.b_base = b0;
+            p.b_end = b0 + nr;
+            const bool chunked = p.n_bc > 1;
+            p.dbias_out = chunked ? reinterpret_cast<float*>(ws + wl.dbp_off) : dbias;
+            p.dbias_stride = chunked ? static_cast<int64_t>(H) * Sq * Sk : 0;
+            p.dbias_accumulate = (!chunked && rg > 0) ? 1 : 0;
+            auto kern = kInplace ? attn_bwd_inplace_kernel<T, 64>
+                                 : attn_bwd_kernel<T, (D < 64 ? D : 32)>;
+            CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device,
+                                     C::kSmemBytes, "attn_bwd"));
+            const int grid = static_cast<int>(std::min<int64_t>(p.items, dev.num_sms));
+            kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, tdq, tdk, tdv, p);
+            CFK_TRY(check_launch("attn_bwd"));
+            if (chunked) {
+                const int64_t n = static_cast<int64_t>(H) * Sq * Sk;
+                const int blocks =
+                    static_cast<int>(std::min<int64_t>((n + 255) / 256, dev.num_sms * 8));
+                dbias_chunks_kernel<<<blocks, 256, 0, st>>>(p.dbias_out, dbias, n, p.n_bc,
+                                                            rg > 0 ? 1 : 0);
+                CFK_TRY(check_launch("attn_bwd dbias chunks"));
+            }
+        }
+        // the range's conversion: in phase 1, or for the last range in phase 2
+        if ((last && (phases & 4)) || (!last && (phases & 2))) {
+            const int64_t rq = nh * Sq * D / 8;
+            const int64_t rkv = nh * Sk * D / 8;
+            const int64_t r0 = static_cast<int64_t>(b0) * H;
+            const ConvertJob job{{dq_acc, dk_acc, dv_acc},
+                                 {dq, dk, dv},
+                                 {rq, rkv, rkv},
+                                 {row_strides(views[5], D), row_strides(views[6], D),
+                                  row_strides(views[7], D)},
+                                 {mqk, mqk, 1.f},
+                                 {r0 * Sq, r0 * Sk, r0 * Sk},
+                                 d8_log2(D)};
+            f32_to_16_kernel<T><<<dev.num_sms * 8, 256, 0, st>>>(job);
+            CFK_TRY(check_launch("attn_bwd convert"));
+        }
+    }
+    return CFK_OK;
 }
 
 template <typename T>
@@ -1494,6 +1557,7 @@ int attn_bwd_entry(const char* fn, int phases, cfk_stream_t stream, cfk_dtype dt
                                    {attn::row_strides(views[5], D), attn::row_strides(views[6], D),
                                     attn::row_strides(views[7], D)},
                                    {1.f, 1.f, 1.f},
+                                   {0, 0, 0},
                                    attn::d8_log2(static_cast<int>(D))};
         attn::f32_to_16_kernel<__half><<<dev.num_sms * 8, 256, 0, st>>>(job);
         return check_launch("attn_bwd zero");

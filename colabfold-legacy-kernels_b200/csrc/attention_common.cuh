@@ -162,14 +162,16 @@ inline int d8_log2(int d) {
 }
 
 // dst_t = (16-bit) (mul_t * src_t) for up to three tensors t in one launch, or zeros where src_t
-// is NULL: src_t packed f32 [N, H, S_t, D] (n8[t] groups of 8 elements), dst_t written through
-// its view.  8 elements per thread and step; D = 8 << d8_log2.
+// is NULL: src_t packed f32 [n, H, S_t, D] (n8[t] groups of 8 elements), dst_t written through
+// its view starting at row row0[t] (rows of a batch-row range).  8 elements per thread and step;
+// D = 8 << d8_log2.
 struct ConvertJob {
     const float* src[3];
     void* dst[3];
     int64_t n8[3];
     RowStrides view[3];
     float mul[3];
+    int64_t row0[3];
     int d8_log2;
 };
 
@@ -198,7 +200,7 @@ __global__ void f32_to_16_kernel(const ConvertJob job) {
             val = make_uint4(E::pack(a.x * m, a.y * m), E::pack(a.z * m, a.w * m),
                              E::pack(b.x * m, b.y * m), E::pack(b.z * m, b.w * m));
         }
-        const int64_t r = k >> job.d8_log2;
+        const int64_t r = (k >> job.d8_log2) + job.row0[t];
         const int c = static_cast<int>(k & ((1 << job.d8_log2) - 1));
         st_global_v4(static_cast<T*>(job.dst[t]) + view_row_offset(job.view[t], r, d) + c * 8,
                      val);

@@ -795,6 +795,7 @@ int attn_fwd_entry(const char* fn, cfk_stream_t stream, cfk_dtype dtype, const v
                                         attn::row_strides(views[3], D),
                                         attn::row_strides(views[3], D)},
                                        {1.f, 1.f, 1.f},
+                                       {0, 0, 0},
                                        attn::d8_log2(static_cast<int>(D))};
             attn::f32_to_16_kernel<__half><<<dev.num_sms * 8, 256, 0, st>>>(job);
             CFK_TRY(check_launch("attn_fwd zero"));

@@ -22,13 +22,16 @@ enum : uint32_t {
     kStatusAborted = 2u,        // another thread of the CTA gave up first
 };
 
-// One word per process and device; read through cfk_device_status().
-extern __device__ uint32_t g_status_word;
-
 // How long a wait may take before it gives up, per device (cfk_set_wait_limit_ns); one second
 // unless changed.
 constexpr unsigned long long kDefaultWaitLimitNs = 1000000000ull;
-extern __device__ unsigned long long g_wait_limit_ns;
+
+// The device status word (one per process and device; read through cfk_device_status()) and
+// the wait limit.  The kernels are compiled as one translation unit (all_kernels.cu) without
+// relocatable device code, which lets ptxas honour setmaxnreg; the variables are defined here,
+// once, in that unit.
+__device__ uint32_t g_status_word = 0;
+__device__ unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
 __device__ __forceinline__ unsigned long long wait_limit_ns() {
     return *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns);
@@ -136,9 +139,11 @@ __device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
 
 // The waiting loop with an explicit limit (ns): gives up when the limit has passed or the
 // CTA's abort word (shared-memory address) is set; giving up sets the abort word and records
-// kStatusTimeoutBarrier in the status word.
-static __device__ __noinline__ bool mbar_wait_limit_s(uint32_t bar, uint32_t parity,
-                                                      uint32_t abort, unsigned long long limit) {
+// kStatusTimeoutBarrier in the status word.  Inlined: an out-of-line call would save and restore
+// the caller's live registers through local memory on every wait that does not complete at
+// once, which in a pipelined kernel is most of them.
+__device__ __forceinline__ bool mbar_wait_limit_s(uint32_t bar, uint32_t parity, uint32_t abort,
+                                                  unsigned long long limit) {
     const unsigned long long t0 = global_ns();
     while (true) {
         if (mbar_try_wait_s(bar, parity)) {
@@ -155,18 +160,13 @@ static __device__ __noinline__ bool mbar_wait_limit_s(uint32_t bar, uint32_t par
     }
 }
 
-static __device__ __noinline__ bool mbar_wait_slow_s(uint32_t bar, uint32_t parity,
-                                                     uint32_t abort) {
-    return mbar_wait_limit_s(bar, parity, abort, wait_limit_ns());
-}
-
 // Waits for the phase with the given parity; gives up like mbar_wait (abort = address of the
-// CTA's abort word).  The slow loop is out of line to keep the caller's registers free.
+// CTA's abort word).
 __device__ __forceinline__ bool mbar_wait_s(uint32_t bar, uint32_t parity, uint32_t abort) {
     if (mbar_try_wait_s(bar, parity)) {
         return true;
     }
-    return mbar_wait_slow_s(bar, parity, abort);
+    return mbar_wait_limit_s(bar, parity, abort, wait_limit_ns());
 }
 
 // mbar_wait_s by every lane of a converged warp, with a warp-uniform result.

@@ -4,9 +4,6 @@
 #include "sm100.cuh"
 
 namespace cfk {
-__device__ uint32_t g_status_word = 0;
-__device__ unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
-
 namespace {
 
 // One CTA of one warp that waits on an mbarrier no thread ever arrives on.  The wait runs the

@@ -93,3 +93,22 @@ def test_bwd_select_path(cuda_device):
     t[4][:, 5] = 0
     t[4][:, 129] = 0
     _check(*t, 0.25, "select path")
+
+
+@pytest.mark.parametrize("shape", [(24, 2, 200, 200, 32), (40, 4, 256, 256, 16)])
+def test_bwd_batch_row_ranges(cuda_device, monkeypatch, shape):
+    """Large problems run the main kernel once per range of batch rows (bounding the f32
+    accumulator workspace), dbias summed across the ranges; a small accumulator budget makes a
+    small problem take that path (with batch chunks inside each range): same results as one
+    launch, and the oracle's."""
+    n, h, sq, sk, d = shape
+    t = _inputs(n, h, sq, sk, d, torch.bfloat16, seed=31 + n)
+    scale = 1.0 / math.sqrt(d)
+    one = _check(*t, scale, "one range")
+    row_bytes = 4 * h * (sq + 2 * sk) * d
+    monkeypatch.setenv("CFK_BWD_RANGE_BYTES", str(5 * row_bytes))  # 5 rows per range
+    ranged = _check(*t, scale, "ranges of 5 rows")
+    for a, b, name in zip(ranged, one, ("dq", "dk", "dv")):
+        # f32 partial sums reduced in a timing-dependent order: equal up to 16-bit rounding
+        assert_close_bf16(a, b, name + " ranges vs one launch", rtol=1e-2, atol=1e-2)
+    assert_close_f32(ranged[3], one[3], "dbias ranges vs one launch")
