@@ -110,6 +110,29 @@ struct FwdParams {
     uint32_t mask_bits;   // bf16 bits of -big, or 0 when masked keys are excluded by select
 };
 
+// (query tile, head, row group) of work item `item`, query tile fastest.  Item counts below
+// 2^32 (every practical launch) take 32-bit divisions, which cost a fraction of 64-bit ones.
+struct ItemCoords {
+    int qt, h, grp;
+};
+
+__device__ __forceinline__ ItemCoords item_coords(const FwdParams& p, int64_t item) {
+    ItemCoords c;
+    if (p.items < (1ll << 32)) {
+        const uint32_t i = static_cast<uint32_t>(item);
+        const uint32_t rest = i / static_cast<uint32_t>(p.n_qt);
+        c.qt = static_cast<int>(i - rest * static_cast<uint32_t>(p.n_qt));
+        c.grp = static_cast<int>(rest / static_cast<uint32_t>(p.H));
+        c.h = static_cast<int>(rest - static_cast<uint32_t>(c.grp) * static_cast<uint32_t>(p.H));
+    } else {
+        const int64_t rest = item / p.n_qt;
+        c.qt = static_cast<int>(item - rest * p.n_qt);
+        c.grp = static_cast<int>(rest / p.H);
+        c.h = static_cast<int>(rest - static_cast<int64_t>(c.grp) * p.H);
+    }
+    return c;
+}
+
 template <typename T, int D, int NW, bool kBiasTma>
 __global__ void __launch_bounds__(FwdCfg<D, NW>::kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -217,11 +240,8 @@ __global__ void __launch_bounds__(FwdCfg<D, NW>::kThreads, 1)
         // =============================== TMA producer ===============================
         uint32_t g = 0;
         for (int it = 0; it < n_items_mine; ++it) {
-            const int64_t item = blockIdx.x + static_cast<int64_t>(it) * gridDim.x;
-            const int qt = static_cast<int>(item % p.n_qt);
-            const int64_t rest = item / p.n_qt;
-            const int h = static_cast<int>(rest % p.H);
-            const int grp = static_cast<int>(rest / p.H);
+            const ItemCoords ic = item_coords(p, blockIdx.x + static_cast<int64_t>(it) * gridDim.x);
+            const int qt = ic.qt, h = ic.h, grp = ic.grp;
             const int q0 = qt * kBM;
             for (int w = 0; w < NWG; ++w) {
                 const int b = grp * NWG + w;
@@ -336,7 +356,19 @@ __global__ void __launch_bounds__(FwdCfg<D, NW>::kThreads, 1)
             // S(g-1), then P V of the second half of tile g-1, then of the first half of g.
             uint32_t g = 0;
             bool prev_first = false; // tile g - 1 was the first tile of its item
+            bool pend = false;       // P V of half 1 of tile g - 1 (and its stage) outstanding
             for (int it = 0; it < n_items_mine; ++it) {
+                if (pend) {
+                    // The previous item's last P V goes now, not after the next item's q tiles
+                    // arrive: its softmax warpgroups wait for it to normalise and store O.
+                    for (int w = 0; w < NWG; ++w) {
+                        if (!issue_pv(w, g - 1, 1, prev_first)) {
+                            goto done;
+                        }
+                    }
+                    umma_commit(&bars[C::kBarKvEmpty + (g - 1) % NST]);
+                    pend = false;
+                }
                 for (int w = 0; w < NWG; ++w) {
                     if (!mbar_wait_s(BAR(C::kBarQFull + w), it & 1, abort_s)) {
                         goto done;
@@ -352,7 +384,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NW>::kThreads, 1)
                     for (int w = 0; w < NWG; ++w) {
                         if constexpr (C::kAlias) {
                             // S(g) overwrites P(g-1): its last P V goes first (in-order pipe)
-                            if (g > 0 && !issue_pv(w, g - 1, 1, prev_first)) {
+                            if (pend && !issue_pv(w, g - 1, 1, prev_first)) {
                                 goto done;
                             }
                         } else if (g > 0 &&
@@ -377,7 +409,7 @@ __global__ void __launch_bounds__(FwdCfg<D, NW>::kThreads, 1)
                             umma_commit(&bars[C::kBarQEmpty + w]);
                         }
                     }
-                    if (g > 0) {
+                    if (pend) {
                         if constexpr (!C::kAlias) {
                             for (int w = 0; w < NWG; ++w) {
                                 if (!issue_pv(w, g - 1, 1, prev_first)) {
@@ -393,9 +425,10 @@ __global__ void __launch_bounds__(FwdCfg<D, NW>::kThreads, 1)
                         }
                     }
                     prev_first = (t == 0);
+                    pend = true;
                 }
             }
-            if (g > 0) {
+            if (pend) {
                 for (int w = 0; w < NWG; ++w) {
                     if (!issue_pv(w, g - 1, 1, prev_first)) {
                         goto done;
@@ -419,11 +452,8 @@ __global__ void __launch_bounds__(FwdCfg<D, NW>::kThreads, 1)
         const bool always_select = (p.mask_bits == 0);
         uint32_t g = 0;
         for (int it = 0; it < n_items_mine; ++it) {
-            const int64_t item = blockIdx.x + static_cast<int64_t>(it) * gridDim.x;
-            const int qt = static_cast<int>(item % p.n_qt);
-            const int64_t rest = item / p.n_qt;
-            const int h = static_cast<int>(rest % p.H);
-            const int grp = static_cast<int>(rest / p.H);
+            const ItemCoords ic = item_coords(p, blockIdx.x + static_cast<int64_t>(it) * gridDim.x);
+            const int qt = ic.qt, h = ic.h, grp = ic.grp;
             const int b = grp * NWG + w;
             const int row = qt * kBM + r;
 
