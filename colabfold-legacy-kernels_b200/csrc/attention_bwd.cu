@@ -138,6 +138,9 @@ struct BwdCfg {
     // 96 and the other two give theirs down to 48 (4 x 128 x 96 + 2 x 128 x 48 = 768 x 80).
     static constexpr int kDsRegs = 96;
     static constexpr int kOtherRegs = 48;
+    static constexpr int kLaunchRegs = 80;
+    static_assert(4 * kDsRegs + 2 * kOtherRegs == (kThreads / 128) * kLaunchRegs,
+                  "register split");
     static constexpr uint32_t kTmemCols = 512;
     static constexpr int kSCol = 0;
     static constexpr int kDPCol = 128;
@@ -1442,7 +1445,8 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
             auto kern = kInplace ? attn_bwd_inplace_kernel<T, 64>
                                  : attn_bwd_kernel<T, (D < 64 ? D : 32)>;
             CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device,
-                                     C::kSmemBytes, "attn_bwd"));
+                                     C::kSmemBytes, "attn_bwd",
+                                     kInplace ? 0 : BwdCfg<(D < 64 ? D : 32)>::kLaunchRegs));
             const int grid = static_cast<int>(std::min<int64_t>(p.items, dev.num_sms));
             kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, tdq, tdk, tdv, p);
             CFK_TRY(check_launch("attn_bwd"));

@@ -35,15 +35,27 @@ constexpr int kThreads = 320; // 2 epilogue warpgroups + producer warp + MMA war
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 
-// Forward: four epilogue warpgroups (32 output columns each per 128-column chunk); with the
-// fused LayerNorm two (64 columns each), which leaves the LayerNorm warpgroup its registers.
+// Forward: warps 0-15 are four epilogue warpgroups (32 output columns each per 128-column
+// chunk), then the producer and the MMA warp.  With the fused LayerNorm, warpgroups 4 and 5
+// (warps 16-23, 16 rows of a tile each) normalise the x rows and warpgroup 6 holds the
+// producer, the MMA warp and two idle warps; setmaxnreg moves registers from warpgroup 6 to
+// the LayerNorm warps while the epilogue keeps the launch share:
+// 4 x 128 x kEpiRegs + 2 x 128 x kLnRegs + 128 x kMiscRegs = 896 x 72, what the launch gives
+// the block (65536 / 896, in units of 8).
 template <bool kLn>
 struct FwdWarps {
-    static constexpr int kEpiWg = kLn ? 2 : 4;
+    static constexpr int kEpiWg = 4;
     static constexpr int kCols = 128 / kEpiWg;      // output columns per warpgroup and chunk
-    static constexpr int kProducer = 4 * kEpiWg;
+    static constexpr int kLnWarp0 = 16;             // (kLn) first LayerNorm warp
+    static constexpr int kLnWarps = 8;              // (kLn)
+    static constexpr int kLnRows = 128 / kLnWarps;  // rows of a tile per LayerNorm warp
+    static constexpr int kProducer = kLn ? kLnWarp0 + kLnWarps : 16;
     static constexpr int kMma = kProducer + 1;
-    static constexpr int kThreads = (kMma + 1) * 32 + (kLn ? 128 : 0);
+    static constexpr int kThreads = kLn ? 32 * (kProducer + 4) : 576;
+    static constexpr int kLaunchRegs = 72;
+    static constexpr int kEpiRegs = 72, kLnRegs = 88, kMiscRegs = 40; // (kLn)
+    static_assert(!kLn || 4 * kEpiRegs + (kLnWarps / 4) * kLnRegs + kMiscRegs ==
+                              (kThreads / 128) * kLaunchRegs, "register split");
 };
 constexpr int kMaxK = 128;
 constexpr int kWeightBudget = 128 * 1024; // both weight matrices, resident
@@ -118,10 +130,10 @@ struct LnIn {
     float eps;
 };
 
-// kLn: x = LayerNorm(z) is never written to memory.  A fourth warpgroup (warps 10-13, thread =
-// row) reads the z rows of the next tile from global memory while the MMAs of the current one
-// run, normalises them in f32 and writes the 16-bit result straight into the x stage in the
-// swizzled layout the MMA reads; the producer then loads only the weights.
+// kLn: x = LayerNorm(z) is never written to memory.  A LayerNorm warpgroup reads the z rows of
+// the next tile from global memory while the MMAs of the current one run, normalises them in
+// f32 and writes the 16-bit result straight into the x stage in the swizzled layout the MMA
+// reads; the producer then loads only the weights.
 template <typename T, bool kLn>
 __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
     gdp_fwd_kernel(const __grid_constant__ CUtensorMap tm_x,
@@ -159,7 +171,7 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
             mbar_init(&x_empty[i], 1);
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 4 * FW::kEpiWg);
-            mbar_init(&x_ready[i], 4);
+            mbar_init(&x_ready[i], FW::kLnWarps);
         }
         mbar_init(w_full, 1);
         *abort_flag = 0;
@@ -201,7 +213,12 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
     const int n_mine = (n_mt - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                        static_cast<int>(gridDim.x);
 
-    if (warp == kProducerWarp) {
+    if (warp >= kProducerWarp) {
+        // producer and MMA warp (with kLn warpgroup 5, whose registers go to the LayerNorm one)
+        if constexpr (kLn) {
+            setmaxnreg_dec<FW::kMiscRegs>();
+        }
+      if (warp == kProducerWarp) {
         if (lane == 0) {
             // weights once: 64-column atoms of all K rows
             const int atoms = L.npad / 64;
@@ -273,92 +290,129 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
                 umma_commit_w(&x_empty[s]);
             }
         }
-    } else if (kLn && warp > kMmaWarp) {
-        // LayerNorm warpgroup: thread r normalises row r of each tile into the x stage
-        const int r = static_cast<int>(threadIdx.x) - 32 * (kMmaWarp + 1);
+      }
+    } else if (kLn && warp >= FW::kLnWarp0) {
+        // LayerNorm warps.  Warp lw normalises rows [R lw, R lw + R) of each tile (R = kLnRows),
+        // two rows at a time: half h = lane / 16 takes row R lw + 2 j + h of row pair j, lane
+        // cl = lane % 16 its columns [8 cl, 8 cl + 8) (16 bytes: the warp's loads of a row pair
+        // are 512 contiguous bytes).  Row sums go across the 16 lanes by shuffles; gamma and
+        // beta of the lane's columns stay in registers.  The z rows of the next tile are loaded
+        // while the MMAs of the current one run.
+        if constexpr (kLn) {
+            setmaxnreg_inc<FW::kLnRegs>();
+        }
+        const int lw = warp - FW::kLnWarp0;
+        const int h = lane >> 4;
+        const int cl = lane & 15;
         const int nchk = K / 8; // 16-byte chunks of a row
-        const float* gam = reinterpret_cast<const float*>(smem + L.off_ln);
-        const float* bet = gam + kMaxK;
+        const bool col_ok = cl < nchk;
         const float inv_k = 1.0f / static_cast<float>(K);
-        uint4 zr[kMaxK / 8];
-        auto load_row = [&](int i) {
-            const int row = (static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x)) * 128 + r;
-            const uint16_t* src = ln.z + static_cast<int64_t>(row) * K;
+        float2 gam[4], bet[4];
+        {
+            const float* gs = reinterpret_cast<const float*>(smem + L.off_ln);
 #pragma unroll
-            for (int c = 0; c < kMaxK / 8; ++c) {
-                zr[c] = (c < nchk && row < M) ? ld_global_stream_v4(src + 8 * c)
-                                              : make_uint4(0u, 0u, 0u, 0u);
+            for (int e = 0; e < 4; ++e) {
+                const int k0 = col_ok ? 8 * cl + 2 * e : 0;
+                gam[e] = make_float2(gs[k0], gs[k0 + 1]);
+                bet[e] = make_float2(gs[kMaxK + k0], gs[kMaxK + k0 + 1]);
+            }
+        }
+        constexpr int kPairs = FW::kLnRows / 2;
+        uint4 zr[kPairs];
+        auto tile_row = [&](int i, int j) {
+            return (static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x)) * 128 +
+                   FW::kLnRows * lw + 2 * j + h;
+        };
+        auto load_tile = [&](int i) {
+#pragma unroll
+            for (int j = 0; j < kPairs; ++j) {
+                const int row = tile_row(i, j);
+                zr[j] = (col_ok && row < M)
+                            ? ld_global_stream_v4(ln.z + static_cast<int64_t>(row) * K + 8 * cl)
+                            : make_uint4(0u, 0u, 0u, 0u);
             }
         };
         if (n_mine > 0) {
-            load_row(0);
+            load_tile(0);
         }
         for (int i = 0; i < n_mine; ++i) {
             const int s = i % L.xs;
-            const int row = (static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x)) * 128 + r;
-            // two passes over the row in registers: mean, then the centred sum of squares
-            // (f32x2 partial sums in two chains each, so the adds overlap)
-            float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-            for (int c = 0; c < kMaxK / 8; ++c) {
-                if (c < nchk) {
-                    const uint32_t w4[4] = {zr[c].x, zr[c].y, zr[c].z, zr[c].w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        s2[e & 1] = fadd2(s2[e & 1], E::to_float2(w4[e]));
-                    }
-                }
-            }
-            const float mean = ((s2[0].x + s2[0].y) + (s2[1].x + s2[1].y)) * inv_k;
-            const float2 nm2 = make_float2(-mean, -mean);
-            float2 q2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-            for (int c = 0; c < kMaxK / 8; ++c) {
-                if (c < nchk) {
-                    const uint32_t w4[4] = {zr[c].x, zr[c].y, zr[c].z, zr[c].w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 d = fadd2(E::to_float2(w4[e]), nm2);
-                        q2[e & 1] = ffma2(d, d, q2[e & 1]);
-                    }
-                }
-            }
-            const float rstd =
-                rsqrtf(((q2[0].x + q2[0].y) + (q2[1].x + q2[1].y)) * inv_k + ln.eps);
-            // y = (x - mean) rstd gamma + beta = t gamma + beta with t = x rstd - mean rstd;
-            // the packed result replaces z, before waiting for the stage
-            const float2 r2 = make_float2(rstd, rstd);
-            const float2 mr2 = make_float2(-mean * rstd, -mean * rstd);
-#pragma unroll
-            for (int c = 0; c < kMaxK / 8; ++c) {
-                if (c < nchk) {
-                    const uint32_t w4[4] = {zr[c].x, zr[c].y, zr[c].z, zr[c].w};
-                    uint32_t o[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int k0 = 8 * c + 2 * e;
-                        const float2 t = ffma2(E::to_float2(w4[e]), r2, mr2);
-                        const float2 yv = ffma2(t, make_float2(gam[k0], gam[k0 + 1]),
-                                                make_float2(bet[k0], bet[k0 + 1]));
-                        o[e] = E::pack(yv.x, yv.y);
-                    }
-                    zr[c] = make_uint4(o[0], o[1], o[2], o[3]);
-                }
-            }
-            if (row < M) {
-                if (ln.mean) {
-                    ln.mean[row] = mean;
-                }
-                if (ln.rstd) {
-                    ln.rstd[row] = rstd;
-                }
-            }
-            // the z row of the tile after next into L2 (its load below is then an L2 hit)
+            // the warp's rows of the tile after next into L2 (its loads are then L2 hits), one
+            // 128-byte line per lane and step
             if (i + 2 < n_mine) {
-                const int row2 = row + 2 * static_cast<int>(gridDim.x) * 128;
-                if (row2 < M) {
-                    for (int c = 0; c < nchk; c += 8) {
-                        asm volatile("prefetch.global.L2 [%0];" ::"l"(ln.z + static_cast<int64_t>(row2) * K + 8 * c));
+                const int row0 = tile_row(i + 2, 0) - h;
+                const int lines = (FW::kLnRows * K * 2) / 128;
+                for (int ln_i = lane; ln_i < lines; ln_i += 32) {
+                    if (row0 + (ln_i * 64) / K < M) {
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(
+                            ln.z + static_cast<int64_t>(row0) * K + 64 * ln_i));
+                    }
+                }
+            }
+            // two passes in quarters of 4 row pairs (registers): mean, then the centred sum of
+            // squares; each sum is 4 packed adds per lane, then 4 shuffle steps over 16 lanes
+#pragma unroll
+            for (int half = 0; half < kPairs / 4; ++half) {
+                float mean[4], rstd[4];
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    const uint4 v = zr[4 * half + jj];
+                    const float2 a = fadd2(E::to_float2(v.x), E::to_float2(v.y));
+                    const float2 b = fadd2(E::to_float2(v.z), E::to_float2(v.w));
+                    const float2 c = fadd2(a, b);
+                    mean[jj] = c.x + c.y;
+                }
+#pragma unroll
+                for (int o = 1; o < 16; o <<= 1) {
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        mean[jj] += __shfl_xor_sync(0xffffffffu, mean[jj], o);
+                    }
+                }
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    mean[jj] *= inv_k;
+                    const uint4 v = zr[4 * half + jj];
+                    const float2 nm = make_float2(-mean[jj], -mean[jj]);
+                    const float2 d0 = fadd2(E::to_float2(v.x), nm);
+                    const float2 d1 = fadd2(E::to_float2(v.y), nm);
+                    const float2 d2 = fadd2(E::to_float2(v.z), nm);
+                    const float2 d3 = fadd2(E::to_float2(v.w), nm);
+                    float2 q = ffma2(d0, d0, fmul2(d1, d1));
+                    q = ffma2(d2, d2, ffma2(d3, d3, q));
+                    rstd[jj] = col_ok ? q.x + q.y : 0.f; // padding columns are not elements
+                }
+#pragma unroll
+                for (int o = 1; o < 16; o <<= 1) {
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        rstd[jj] += __shfl_xor_sync(0xffffffffu, rstd[jj], o);
+                    }
+                }
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    const int j = 4 * half + jj;
+                    rstd[jj] = rsqrtf(rstd[jj] * inv_k + ln.eps);
+                    // y = (x - mean) rstd gamma + beta = t gamma + beta, t = x rstd - mean rstd
+                    const float2 r2 = make_float2(rstd[jj], rstd[jj]);
+                    const float2 mr2 = make_float2(-mean[jj] * rstd[jj], -mean[jj] * rstd[jj]);
+                    const uint32_t w4[4] = {zr[j].x, zr[j].y, zr[j].z, zr[j].w};
+                    uint32_t o4[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 t = ffma2(E::to_float2(w4[e]), r2, mr2);
+                        const float2 yv = ffma2(t, gam[e], bet[e]);
+                        o4[e] = E::pack(yv.x, yv.y);
+                    }
+                    zr[j] = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+                    const int row = tile_row(i, j);
+                    if (cl == 0 && row < M) {
+                        if (ln.mean) {
+                            ln.mean[row] = mean[jj];
+                        }
+                        if (ln.rstd) {
+                            ln.rstd[row] = rstd[jj];
+                        }
                     }
                 }
             }
@@ -366,12 +420,14 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
             if (i >= L.xs && !mbar_wait(&x_empty[s], ((i / L.xs) - 1) & 1, abort_flag)) {
                 goto done;
             }
-            const uint32_t xrow = sbase + L.off_x + s * L.x_stage + r * 128;
+            if (col_ok) {
+                const uint32_t xs0 = sbase + L.off_x + s * L.x_stage;
 #pragma unroll
-            for (int c = 0; c < kMaxK / 8; ++c) {
-                if (c < nchk) {
-                    // chunk c: panel c / 8, 16-byte chunk c % 8 of the row (128-byte swizzle)
-                    attn::sts128(xrow + (c >> 3) * 16384 + ((((c & 7) ^ (r & 7))) << 4), zr[c]);
+                for (int j = 0; j < kPairs; ++j) {
+                    // row r, 16-byte chunk cl: panel cl / 8, chunk cl % 8 (128-byte swizzle)
+                    const int r = FW::kLnRows * lw + 2 * j + h;
+                    attn::sts128(xs0 + r * 128 + (cl >> 3) * 16384 + (((cl & 7) ^ (r & 7)) << 4),
+                                 zr[j]);
                 }
             }
             fence_proxy_async_smem();
@@ -380,7 +436,7 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
                 mbar_arrive(&x_ready[s]);
             }
             if (i + 1 < n_mine) {
-                load_row(i + 1); // in flight while the MMAs of this tile run
+                load_tile(i + 1); // in flight while the MMAs of this tile run
             }
         }
     } else {
@@ -463,7 +519,7 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
     }
 done:
     __syncwarp();
-    if (warp < kProducerWarp && (threadIdx.x & 127) == 0) {
+    if (warp < 4 * FW::kEpiWg && (threadIdx.x & 127) == 0) {
         bulk_wait<0>(); // no store may still read the staging boxes (also on the abort path)
     }
     if (*abort_flag) {
@@ -546,17 +602,19 @@ int gdp_fwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const vo
     }
     CUtensorMap tx, twp, twg, tout;
     // x [M, K]: dims (K, M, 1), box 64 x 128; weights [K, N]: dims (N, K, 1), box 64 x K;
-    // out [M, N]: dims (N, M, 1), box kCols x 128 (stores; 64 with the fused LayerNorm, else 32)
+    // out [M, N]: dims (N, M, 1), box 32 x 128 (stores)
     CFK_TRY(make_tmap_3d(&tx, ln ? ln->z : x, K, M, 1, 2ull * K, 2ull * K * M, 64, 128, 1, 128,
                          "gdp x"));
     CFK_TRY(make_tmap_3d(&twp, wp, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wp"));
     CFK_TRY(make_tmap_3d(&twg, wg, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "gdp wg"));
-    const int out_cols = ln ? FwdWarps<true>::kCols : FwdWarps<false>::kCols;
+    constexpr int out_cols = FwdWarps<true>::kCols;
+    static_assert(FwdWarps<true>::kCols == FwdWarps<false>::kCols, "one store box width");
     CFK_TRY(make_tmap_3d(&tout, out, N, M, 1, 2ull * N, 2ull * N * M, out_cols, 128, 1,
                          2 * out_cols, "gdp out"));
     auto kern = ln ? gdp_fwd_kernel<T, true> : gdp_fwd_kernel<T, false>;
     CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
-                             ln ? "gdp_fwd_ln" : "gdp_fwd"));
+                             ln ? "gdp_fwd_ln" : "gdp_fwd",
+                             ln ? FwdWarps<true>::kLaunchRegs : 0));
     const int n_mt = (M + 127) / 128;
     const int grid = std::min(n_mt, dev.num_sms);
     const LnIn none{};

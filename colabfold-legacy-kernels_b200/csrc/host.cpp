@@ -80,11 +80,27 @@ int current_device(DeviceInfo* info) {
     return CFK_OK;
 }
 
-int ensure_smem_attr(const void* kernel, int device, int bytes, const char* name) {
+int ensure_smem_attr(const void* kernel, int device, int bytes, const char* name,
+                     int launch_regs) {
     std::lock_guard<std::mutex> lock(g_attr_mu);
     auto key = std::make_pair(kernel, device);
     if (g_attr_done.count(key)) {
         return CFK_OK;
+    }
+    if (launch_regs > 0) {
+        // setmaxnreg.inc waits until the block's pool (threads x registers at launch) has the
+        // registers: a kernel compiled with fewer than the split assumes must not launch
+        cudaFuncAttributes a{};
+        cudaError_t e = cudaFuncGetAttributes(&a, kernel);
+        if (e != cudaSuccess) {
+            return fail(CFK_ERR_LAUNCH, "%s: cudaFuncGetAttributes: %s", name,
+                        cudaGetErrorString(e));
+        }
+        if (a.numRegs != launch_regs) {
+            return fail(CFK_ERR_LAUNCH,
+                        "%s: built with %d registers per thread; its register split needs %d",
+                        name, a.numRegs, launch_regs);
+        }
     }
     cudaError_t e =
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

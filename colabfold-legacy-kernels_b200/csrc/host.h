@@ -30,7 +30,10 @@ struct DeviceInfo {
 int current_device(DeviceInfo* info);
 
 // Sets cudaFuncAttributeMaxDynamicSharedMemorySize once per (kernel, device).
-int ensure_smem_attr(const void* kernel, int device, int bytes, const char* name);
+// launch_regs > 0: the kernel moves registers between its warpgroups with setmaxnreg and must
+// have been built with exactly that many registers per thread (checked once, else an error).
+int ensure_smem_attr(const void* kernel, int device, int bytes, const char* name,
+                     int launch_regs = 0);
 
 // Maps cudaGetLastError() after a launch onto CFK_ERR_LAUNCH.
 int check_launch(const char* what);
