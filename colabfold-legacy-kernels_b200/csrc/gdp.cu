@@ -78,7 +78,7 @@ struct FwdLayout {
     int npad;      // N rounded up to 128
     int x_stage;   // one x tile: ceil(K/64) panels of 128 rows x 128 B
     int xs;        // x stages (2 when they fit beside the weights, else 1)
-    int off_x, off_wp, off_wg, off_bp, off_bg, off_ones, off_stg, off_ln, off_bar, total;
+    int off_x, off_w, off_b, off_ones, off_stg, off_ln, off_bar, total;
 };
 
 __host__ __device__ inline FwdLayout fwd_layout(int K, int N) {
@@ -88,11 +88,12 @@ __host__ __device__ inline FwdLayout fwd_layout(int K, int N) {
     L.x_stage = ((K + 63) / 64) * 16384;
     for (L.xs = 2; L.xs >= 1; --L.xs) {
         L.off_x = 0;
-        L.off_wp = L.xs * L.x_stage;
-        L.off_wg = L.off_wp + L.kb * L.npad * 2;
-        L.off_bp = L.off_wg + L.kb * L.npad * 2;
-        L.off_bg = L.off_bp + (L.npad / 8) * 256;
-        L.off_ones = L.off_bg + (L.npad / 8) * 256;
+        // weights per 128-column chunk c: the 64-column atoms wp 2c, wp 2c+1, wg 2c, wg 2c+1
+        // (kb rows x 128 B each), so one N = 256 MMA per k-step makes [p | g] of the chunk
+        L.off_w = L.xs * L.x_stage;
+        // bias operand, per chunk: the 16 column groups of bp, then those of bg
+        L.off_b = L.off_w + 2 * L.kb * L.npad * 2;
+        L.off_ones = L.off_b + 2 * (L.npad / 8) * 256;
         L.off_stg = L.off_ones + 4096; // output staging: one [128 x 64] box per warpgroup
         L.off_ln = L.off_stg + 2 * 16384; // LayerNorm gamma, beta (f32 [K] each), fused form
         L.off_bar = L.off_ln + 2 * kMaxK * 4;
@@ -109,13 +110,13 @@ __host__ __device__ inline FwdLayout fwd_layout(int K, int N) {
 __device__ __forceinline__ uint64_t x_desc(uint32_t x, int s) {
     return smem_desc(x + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024, kSwizzle128);
 }
-// weight [K rows x n] stored as 64-column atoms of kb rows x 128 B, MN-major, columns
-// [128c, 128c + 128), k-step s.
+// weight [K rows x n] stored as 64-column atoms of kb rows x 128 B, MN-major, from atom 2c
+// on (as many atoms as the MMA's N spans), k-step s.
 __device__ __forceinline__ uint64_t w_desc(uint32_t w, int kb, int c, int s) {
     return smem_desc(w + 2 * c * (kb * 128) + s * 2048, kb * 128, 1024, kSwizzle128);
 }
-// bias row operand [16 x npad] (row 0 = bias), MN-major interleave: (kk, n) at
-// (n/8)*256 + kk*16 + (n%8)*2; columns [128c, 128c + 128).
+// bias row operand [16 x n] (row 0 = bias), MN-major interleave: (kk, n) at
+// (n/8)*256 + kk*16 + (n%8)*2; from column 128c on.
 __device__ __forceinline__ uint64_t brow_desc(uint32_t b, int c) {
     return smem_desc(b + c * 16 * 256, 128, 256, kInterleave);
 }
@@ -179,15 +180,14 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
     }
     // bias rows (row 0 = bias, rows 1..15 = 0) and ones[128 x 16] (column 0 = 1), in T
     {
-        uint16_t* sbp = reinterpret_cast<uint16_t*>(smem + L.off_bp);
-        uint16_t* sbg = reinterpret_cast<uint16_t*>(smem + L.off_bg);
-        const int nel = (L.npad / 8) * 128; // 16-bit elements per bias operand
+        uint16_t* sb = reinterpret_cast<uint16_t*>(smem + L.off_b);
+        const int nel = 2 * (L.npad / 8) * 128; // 16-bit elements of the bias operand
         for (int i = threadIdx.x; i < nel; i += blockDim.x) {
-            const int chunk = i / 128, within = i % 128, kk = within / 8, e = within % 8;
-            const int n = chunk * 8 + e;
+            const int grp = i / 128, within = i % 128, kk = within / 8, e = within % 8;
+            const int c = grp / 32, t = (grp / 16) & 1; // chunk; 0 = bp, 1 = bg
+            const int n = c * 128 + (grp & 15) * 8 + e;
             const bool on = (kk == 0 && n < N);
-            sbp[i] = on ? bp[n] : uint16_t(0);
-            sbg[i] = on ? bg[n] : uint16_t(0);
+            sb[i] = on ? (t ? bg[n] : bp[n]) : uint16_t(0);
         }
         const uint32_t one = E::kBf16 ? 0x3F80u : 0x3C00u;
         uint32_t* ones = reinterpret_cast<uint32_t*>(smem + L.off_ones);
@@ -224,8 +224,10 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
             const int atoms = L.npad / 64;
             mbar_arrive_expect_tx(w_full, 2 * atoms * L.kb * 128);
             for (int a = 0; a < atoms; ++a) {
-                tma_load_3d(smem + L.off_wp + a * L.kb * 128, &tm_wp, w_full, a * 64, 0, 0);
-                tma_load_3d(smem + L.off_wg + a * L.kb * 128, &tm_wg, w_full, a * 64, 0, 0);
+                const int slot = 4 * (a >> 1) + (a & 1); // wp atom a; wg atom a two further
+                tma_load_3d(smem + L.off_w + slot * L.kb * 128, &tm_wp, w_full, a * 64, 0, 0);
+                tma_load_3d(smem + L.off_w + (slot + 2) * L.kb * 128, &tm_wg, w_full, a * 64, 0,
+                            0);
             }
             const int panels = (K + 63) / 64;
             for (int i = 0; i < (kLn ? 0 : n_mine); ++i) {
@@ -251,8 +253,7 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
     } else if (warp == kMmaWarp) {
         // whole warp, converged: MMAs and commits are elect.sync-issued
         {
-            constexpr uint32_t kId = idesc_f16(128, 128, false, true, E::kBf16);
-            constexpr uint32_t kIdBias = idesc_f16(128, 128, false, true, E::kBf16);
+            constexpr uint32_t kId = idesc_f16(128, 256, false, true, E::kBf16);
             const uint64_t ones = attn::interleave16_kmajor(sbase + L.off_ones);
             const int ksteps = K / 16;
             if (!mbar_wait_w(w_full, 0, abort_flag)) {
@@ -273,18 +274,13 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
                         goto done;
                     }
                     tc_fence_after();
-                    const uint32_t accp = tmem + bf * 256;
-                    const uint32_t accg = accp + 128;
+                    // [p | g] of chunk c: columns [0, 128) p, [128, 256) g
+                    const uint32_t acc = tmem + bf * 256;
                     for (int ks = 0; ks < ksteps; ++ks) {
-                        umma_ss_w(accp, x_desc(x, ks), w_desc(sbase + L.off_wp, L.kb, c, ks), kId,
-                                ks > 0);
+                        umma_ss_w(acc, x_desc(x, ks), w_desc(sbase + L.off_w, L.kb, 2 * c, ks),
+                                  kId, ks > 0);
                     }
-                    umma_ss_w(accp, ones, brow_desc(sbase + L.off_bp, c), kIdBias, 1);
-                    for (int ks = 0; ks < ksteps; ++ks) {
-                        umma_ss_w(accg, x_desc(x, ks), w_desc(sbase + L.off_wg, L.kb, c, ks), kId,
-                                ks > 0);
-                    }
-                    umma_ss_w(accg, ones, brow_desc(sbase + L.off_bg, c), kIdBias, 1);
+                    umma_ss_w(acc, ones, brow_desc(sbase + L.off_b, 2 * c), kId, 1);
                     umma_commit_w(&acc_full[bf]);
                 }
                 umma_commit_w(&x_empty[s]);
