@@ -10,3 +10,4 @@
 #include "attention_bwd.cu"
 #include "gdp.cu"
 #include "gate.cu"
+#include "linear.cu"

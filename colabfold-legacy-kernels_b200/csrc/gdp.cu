@@ -81,7 +81,8 @@ struct FwdLayout {
     int off_x, off_w, off_b, off_ones, off_stg, off_ln, off_bar, total;
 };
 
-__host__ __device__ inline FwdLayout fwd_layout(int K, int N) {
+// gate = false: the plain projection (one weight matrix, one bias operand).
+__host__ __device__ inline FwdLayout fwd_layout(int K, int N, bool gate = true) {
     FwdLayout L;
     L.kb = K;
     L.npad = (N + 127) / 128 * 128;
@@ -92,8 +93,8 @@ __host__ __device__ inline FwdLayout fwd_layout(int K, int N) {
         // (kb rows x 128 B each), so one N = 256 MMA per k-step makes [p | g] of the chunk
         L.off_w = L.xs * L.x_stage;
         // bias operand, per chunk: the 16 column groups of bp, then those of bg
-        L.off_b = L.off_w + 2 * L.kb * L.npad * 2;
-        L.off_ones = L.off_b + 2 * (L.npad / 8) * 256;
+        L.off_b = L.off_w + (gate ? 2 : 1) * L.kb * L.npad * 2;
+        L.off_ones = L.off_b + (gate ? 2 : 1) * (L.npad / 8) * 256;
         L.off_stg = L.off_ones + 4096; // output staging: one [128 x 64] box per warpgroup
         L.off_ln = L.off_stg + 2 * 16384; // LayerNorm gamma, beta (f32 [K] each), fused form
         L.off_bar = L.off_ln + 2 * kMaxK * 4;
@@ -135,19 +136,23 @@ struct LnIn {
 // the next tile from global memory while the MMAs of the current one run, normalises them in
 // f32 and writes the 16-bit result straight into the x stage in the swizzled layout the MMA
 // reads; the producer then loads only the weights.
-template <typename T, bool kLn>
+//
+// kGate = false: the plain projection y = x wp + bp (bp may be null), columns [0, n_split) to
+// tm_out and [n_split, N) to tm_out2 (n_split a multiple of 128); wg, bg and mask are unused.
+template <typename T, bool kLn, bool kGate>
 __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
     gdp_fwd_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_wp,
                    const __grid_constant__ CUtensorMap tm_wg,
-                   const __grid_constant__ CUtensorMap tm_out, const uint16_t* __restrict__ bp,
-                   const uint16_t* __restrict__ bg, const uint16_t* __restrict__ mask, int M,
-                   int K, int N, const LnIn ln) {
+                   const __grid_constant__ CUtensorMap tm_out,
+                   const __grid_constant__ CUtensorMap tm_out2, int n_split,
+                   const uint16_t* __restrict__ bp, const uint16_t* __restrict__ bg,
+                   const uint16_t* __restrict__ mask, int M, int K, int N, const LnIn ln) {
     using E = Elem<T>;
     using FW = FwdWarps<kLn>;
     constexpr int kProducerWarp = FW::kProducer;
     constexpr int kMmaWarp = FW::kMma;
-    const FwdLayout L = fwd_layout(K, N);
+    const FwdLayout L = fwd_layout(K, N, kGate);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -181,12 +186,16 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
     // bias rows (row 0 = bias, rows 1..15 = 0) and ones[128 x 16] (column 0 = 1), in T
     {
         uint16_t* sb = reinterpret_cast<uint16_t*>(smem + L.off_b);
-        const int nel = 2 * (L.npad / 8) * 128; // 16-bit elements of the bias operand
+        const int nel = (kGate ? 2 : 1) * (L.npad / 8) * 128; // 16-bit elements of the operand
         for (int i = threadIdx.x; i < nel; i += blockDim.x) {
             const int grp = i / 128, within = i % 128, kk = within / 8, e = within % 8;
-            const int c = grp / 32, t = (grp / 16) & 1; // chunk; 0 = bp, 1 = bg
-            const int n = c * 128 + (grp & 15) * 8 + e;
-            const bool on = (kk == 0 && n < N);
+            int n = grp * 8 + e, t = 0;
+            if constexpr (kGate) {
+                const int c = grp / 32; // chunk; t: 0 = bp, 1 = bg
+                t = (grp / 16) & 1;
+                n = c * 128 + (grp & 15) * 8 + e;
+            }
+            const bool on = (kk == 0 && n < N && bp != nullptr);
             sb[i] = on ? (t ? bg[n] : bp[n]) : uint16_t(0);
         }
         const uint32_t one = E::kBf16 ? 0x3F80u : 0x3C00u;
@@ -222,12 +231,17 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
         if (lane == 0) {
             // weights once: 64-column atoms of all K rows
             const int atoms = L.npad / 64;
-            mbar_arrive_expect_tx(w_full, 2 * atoms * L.kb * 128);
+            mbar_arrive_expect_tx(w_full, (kGate ? 2 : 1) * atoms * L.kb * 128);
             for (int a = 0; a < atoms; ++a) {
-                const int slot = 4 * (a >> 1) + (a & 1); // wp atom a; wg atom a two further
-                tma_load_3d(smem + L.off_w + slot * L.kb * 128, &tm_wp, w_full, a * 64, 0, 0);
-                tma_load_3d(smem + L.off_w + (slot + 2) * L.kb * 128, &tm_wg, w_full, a * 64, 0,
-                            0);
+                if constexpr (kGate) {
+                    const int slot = 4 * (a >> 1) + (a & 1); // wp atom a; wg atom a two further
+                    tma_load_3d(smem + L.off_w + slot * L.kb * 128, &tm_wp, w_full, a * 64, 0,
+                                0);
+                    tma_load_3d(smem + L.off_w + (slot + 2) * L.kb * 128, &tm_wg, w_full,
+                                a * 64, 0, 0);
+                } else {
+                    tma_load_3d(smem + L.off_w + a * L.kb * 128, &tm_wp, w_full, a * 64, 0, 0);
+                }
             }
             const int panels = (K + 63) / 64;
             for (int i = 0; i < (kLn ? 0 : n_mine); ++i) {
@@ -253,7 +267,8 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
     } else if (warp == kMmaWarp) {
         // whole warp, converged: MMAs and commits are elect.sync-issued
         {
-            constexpr uint32_t kId = idesc_f16(128, 256, false, true, E::kBf16);
+            constexpr uint32_t kId = idesc_f16(128, kGate ? 256 : 128, false, true, E::kBf16);
+            constexpr int kAtomStep = kGate ? 2 : 1; // 128-column groups per chunk operand
             const uint64_t ones = attn::interleave16_kmajor(sbase + L.off_ones);
             const int ksteps = K / 16;
             if (!mbar_wait_w(w_full, 0, abort_flag)) {
@@ -274,13 +289,14 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
                         goto done;
                     }
                     tc_fence_after();
-                    // [p | g] of chunk c: columns [0, 128) p, [128, 256) g
+                    // [p | g] of chunk c: columns [0, 128) p, [128, 256) g (the plain
+                    // projection: columns [0, 128))
                     const uint32_t acc = tmem + bf * 256;
                     for (int ks = 0; ks < ksteps; ++ks) {
-                        umma_ss_w(acc, x_desc(x, ks), w_desc(sbase + L.off_w, L.kb, 2 * c, ks),
-                                  kId, ks > 0);
+                        umma_ss_w(acc, x_desc(x, ks),
+                                  w_desc(sbase + L.off_w, L.kb, kAtomStep * c, ks), kId, ks > 0);
                     }
-                    umma_ss_w(acc, ones, brow_desc(sbase + L.off_b, 2 * c), kId, 1);
+                    umma_ss_w(acc, ones, brow_desc(sbase + L.off_b, kAtomStep * c), kId, 1);
                     umma_commit_w(&acc_full[bf]);
                 }
                 umma_commit_w(&x_empty[s]);
@@ -454,7 +470,7 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
             const int mt = blockIdx.x + i * gridDim.x;
             const int row = mt * 128 + r;
             const bool row_ok = row < M;
-            const float hm = row_ok ? 0.5f * E::to_float(mask[row]) : 0.f;
+            const float hm = (kGate && row_ok) ? 0.5f * E::to_float(mask[row]) : 0.f;
             for (int c = 0; c < n_chunks; ++c, ++chunk_ctr) {
                 const int bf = chunk_ctr & 1;
                 const bool ok = mbar_wait(&acc_full[bf], (chunk_ctr >> 1) & 1, abort_flag);
@@ -473,7 +489,9 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
                 for (int q = 0; q < kCols / 16; ++q) {
                     uint32_t pv[16], gv[16];
                     tmem_ld16(accp + 16 * q, pv);
-                    tmem_ld16(accg + 16 * q, gv);
+                    if constexpr (kGate) {
+                        tmem_ld16(accg + 16 * q, gv);
+                    }
                     tmem_ld_wait();
                     uint32_t o[8];
 #pragma unroll
@@ -482,10 +500,14 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
                             const float p = __uint_as_float(pv[2 * e + h]);
-                            const float g = __uint_as_float(gv[2 * e + h]);
-                            float t;
-                            asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * g));
-                            y[h] = p * fmaf(hm, t, hm); // mask * p * (0.5 tanh(g/2) + 0.5)
+                            if constexpr (kGate) {
+                                const float g = __uint_as_float(gv[2 * e + h]);
+                                float t;
+                                asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * g));
+                                y[h] = p * fmaf(hm, t, hm); // mask * p * (0.5 tanh(g/2) + 0.5)
+                            } else {
+                                y[h] = p;
+                            }
                         }
                         o[e] = E::pack(y[0], y[1]);
                     }
@@ -503,8 +525,15 @@ __global__ void __launch_bounds__(FwdWarps<kLn>::kThreads, 1)
                 fence_proxy_async_smem();
                 named_bar_sync(1 + w, 128);
                 if (leader) {
-                    tma_store_3d(&tm_out, sbase + L.off_stg + w * 128 * kRowB,
-                                 c * 128 + kCols * w, mt * 128, 0);
+                    const int col = c * 128 + kCols * w;
+                    // (columns past N, in the last chunk's padding, are clipped by tm_out)
+                    if (kGate || n_split >= N || col < n_split) {
+                        tma_store_3d(&tm_out, sbase + L.off_stg + w * 128 * kRowB, col, mt * 128,
+                                     0);
+                    } else {
+                        tma_store_3d(&tm_out2, sbase + L.off_stg + w * 128 * kRowB,
+                                     col - n_split, mt * 128, 0);
+                    }
                     bulk_commit();
                 }
             }
@@ -569,10 +598,10 @@ __global__ void gdp_fwd_generic_kernel(const uint16_t* __restrict__ x,
     }
 }
 
-bool fwd_fast_shape(int K, int N) {
-    const FwdLayout L = fwd_layout(K, N);
-    return (K % 16 == 0) && K >= 16 && K <= kMaxK && 2 * L.kb * L.npad * 2 <= kWeightBudget &&
-           L.total <= 227 * 1024;
+bool fwd_fast_shape(int K, int N, bool gate = true) {
+    const FwdLayout L = fwd_layout(K, N, gate);
+    return (K % 16 == 0) && K >= 16 && K <= kMaxK &&
+           (gate ? 2 : 1) * L.kb * L.npad * 2 <= kWeightBudget && L.total <= 227 * 1024;
 }
 
 // ln != nullptr: x is LayerNorm(ln->z) and only the fused tcgen05 kernel may be used (the
@@ -607,7 +636,7 @@ int gdp_fwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const vo
     static_assert(FwdWarps<true>::kCols == FwdWarps<false>::kCols, "one store box width");
     CFK_TRY(make_tmap_3d(&tout, out, N, M, 1, 2ull * N, 2ull * N * M, out_cols, 128, 1,
                          2 * out_cols, "gdp out"));
-    auto kern = ln ? gdp_fwd_kernel<T, true> : gdp_fwd_kernel<T, false>;
+    auto kern = ln ? gdp_fwd_kernel<T, true, true> : gdp_fwd_kernel<T, false, true>;
     CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
                              ln ? "gdp_fwd_ln" : "gdp_fwd",
                              ln ? FwdWarps<true>::kLaunchRegs : 0));
@@ -615,9 +644,79 @@ int gdp_fwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const vo
     const int grid = std::min(n_mt, dev.num_sms);
     const LnIn none{};
     kern<<<grid, ln ? FwdWarps<true>::kThreads : FwdWarps<false>::kThreads, L.total, st>>>(
-        tx, twp, twg, tout, static_cast<const uint16_t*>(bp), static_cast<const uint16_t*>(bg),
-        static_cast<const uint16_t*>(mask), M, K, N, ln ? *ln : none);
+        tx, twp, twg, tout, tout, N, static_cast<const uint16_t*>(bp),
+        static_cast<const uint16_t*>(bg), static_cast<const uint16_t*>(mask), M, K, N,
+        ln ? *ln : none);
     return check_launch(ln ? "gdp_fwd_ln" : "gdp_fwd");
+}
+
+// y = x w + b on CUDA cores (shapes or alignments the tcgen05 kernel does not take); columns
+// [0, n_split) to y0 (row stride ld0), [n_split, N) to y1 (row stride ld1).
+template <typename T>
+__global__ void linear_fwd_generic_kernel(const uint16_t* __restrict__ x,
+                                          const uint16_t* __restrict__ w,
+                                          const uint16_t* __restrict__ b, uint16_t* y0,
+                                          int64_t ld0, uint16_t* y1, int64_t ld1, int n_split,
+                                          int M, int K, int N) {
+    using E = Elem<T>;
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int m = blockIdx.y * blockDim.y + threadIdx.y;
+    if (m >= M || n >= N) {
+        return;
+    }
+    float a = b ? E::to_float(b[n]) : 0.f;
+    for (int k = 0; k < K; ++k) {
+        a = fmaf(E::to_float(x[static_cast<int64_t>(m) * K + k]),
+                 E::to_float(w[static_cast<int64_t>(k) * N + n]), a);
+    }
+    if (n < n_split) {
+        y0[m * ld0 + n] = E::from_float(a);
+    } else {
+        y1[m * ld1 + (n - n_split)] = E::from_float(a);
+    }
+}
+
+// The plain projection: y = x w + b (b may be null), columns [0, n_split) into y0 with row
+// stride ld0 elements and [n_split, N) into y1 with row stride ld1.
+template <typename T>
+int linear_fwd_impl(cudaStream_t st, const DeviceInfo& dev, const void* x, const void* w,
+                    const void* b, void* y0, int64_t ld0, void* y1, int64_t ld1, int n_split,
+                    int M, int K, int N) {
+    const FwdLayout L = fwd_layout(K, N, false);
+    const bool fast = fwd_fast_shape(K, N, false) && (n_split == N || n_split % 128 == 0) &&
+                      aligned16(x) &&
+                      aligned16(w) && aligned16(y0) && ld0 % 8 == 0 &&
+                      (n_split == N || (aligned16(y1) && ld1 % 8 == 0));
+    if (!fast) {
+        dim3 block(16, 16), grid((N + 15) / 16, (M + 15) / 16);
+        linear_fwd_generic_kernel<T><<<grid, block, 0, st>>>(
+            static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w),
+            static_cast<const uint16_t*>(b), static_cast<uint16_t*>(y0), ld0,
+            static_cast<uint16_t*>(y1), ld1, n_split, M, K, N);
+        return check_launch("linear_fwd_generic");
+    }
+    CUtensorMap tx, tw, ty0, ty1;
+    constexpr int out_cols = FwdWarps<false>::kCols;
+    CFK_TRY(make_tmap_3d(&tx, x, K, M, 1, 2ull * K, 2ull * K * M, 64, 128, 1, 128, "linear x"));
+    CFK_TRY(make_tmap_3d(&tw, w, N, K, 1, 2ull * N, 2ull * N * K, 64, K, 1, 128, "linear w"));
+    CFK_TRY(make_tmap_3d(&ty0, y0, n_split, M, 1, 2ull * ld0, 2ull * ld0 * M, out_cols, 128, 1,
+                         2 * out_cols, "linear y0"));
+    if (n_split < N) {
+        CFK_TRY(make_tmap_3d(&ty1, y1, N - n_split, M, 1, 2ull * ld1, 2ull * ld1 * M, out_cols,
+                             128, 1, 2 * out_cols, "linear y1"));
+    } else {
+        ty1 = ty0;
+    }
+    auto kern = gdp_fwd_kernel<T, false, false>;
+    CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, 227 * 1024,
+                             "linear_fwd"));
+    const int n_mt = (M + 127) / 128;
+    const int grid = std::min(n_mt, dev.num_sms);
+    const LnIn none{};
+    kern<<<grid, FwdWarps<false>::kThreads, L.total, st>>>(
+        tx, tw, tw, ty0, ty1, n_split, static_cast<const uint16_t*>(b), nullptr, nullptr, M, K,
+        N, none);
+    return check_launch("linear_fwd");
 }
 
 // ==========================================================================================

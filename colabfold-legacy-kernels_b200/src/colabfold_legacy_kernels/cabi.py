@@ -54,6 +54,19 @@ def views(*strides):
 
 _views = ctypes.POINTER(View)
 
+
+class LinearSeg(ctypes.Structure):
+    """cfk_linear_seg: one column block of a projection's output gradient."""
+    _fields_ = [("dy", _vp), ("ld", _i64), ("n", _i64), ("w", _vp), ("dw", _vp), ("db", _vp)]
+
+
+def linear_segs(*segs):
+    """A cfk_linear_seg array from (dy, ld, n, w, dw, db) tuples of pointers and sizes."""
+    return (LinearSeg * len(segs))(*[LinearSeg(*s) for s in segs])
+
+
+_segs = ctypes.POINTER(LinearSeg)
+
 # name -> argtypes (restype is int for all but the two string getters)
 SIGNATURES = {
     "cfk_attn_fwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
@@ -85,6 +98,10 @@ SIGNATURES = {
     "cfk_gdp_bwd_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
     "cfk_gdp_bwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                     _vp, _sz, _i64, _i64, _i64],
+    "cfk_linear_fwd": [_vp, _int, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64],
+    "cfk_linear_bwd_dx": [_vp, _int, _segs, _int, _vp, _i64, _i64],
+    "cfk_linear_bwd_dw_workspace_size": [_segs, _int, _i64, _i64, ctypes.POINTER(_sz)],
+    "cfk_linear_bwd_dw": [_vp, _int, _vp, _segs, _int, _i64, _i64, _vp, _sz],
     "cfk_device_status": [ctypes.POINTER(ctypes.c_uint32)],
     "cfk_clear_device_status": [],
     "cfk_set_wait_limit_ns": [ctypes.c_uint64],

@@ -7,6 +7,8 @@ These exist for tests, benchmarks and PyTorch users; XLA users go through the FF
 
 import os
 
+import ctypes
+
 import torch
 
 from . import cabi
@@ -254,6 +256,97 @@ def gdp_bwd(x, wp, bp, wg, bg, mask, dout, workspace=None, grads=None):
                   _ptr(dwg), _ptr(dbg), _ptr(workspace), workspace.numel(), m, k, n)
     _done(x.device)
     return dx, dwp, dbp, dwg, dbg
+
+
+def _row_stride(t):
+    """Row stride of a 2-D tensor whose rows may be strided (a column block of a wider buffer,
+    e.g. q of a [M, 3*H*D] projection): the last axis must be contiguous."""
+    if not t.is_cuda:
+        raise ValueError("tensors must be on a CUDA device")
+    if t.dim() != 2 or (t.stride(1) != 1 and t.shape[1] > 1):
+        raise ValueError("expected a 2-D tensor with a contiguous last axis")
+    return t.stride(0) if t.shape[0] > 1 else t.shape[1]
+
+
+def linear_fwd(x, w, b=None, out=None):
+    """y = x w + b (cfk_linear_fwd): x [M,K], w [K,N] contiguous, b [N] or None, 16-bit.
+    out: None (a new [M,N] tensor), one [M,N] tensor whose rows may be strided, or a pair
+    (y0 [M, n0], y1 [M, N - n0]) of such tensors (n0 a multiple of 128) that receive columns
+    [0, n0) and [n0, N).  Returns out (the pair when a pair was given)."""
+    _check(x, w, b)
+    m, k = x.shape
+    n = w.shape[1]
+    if w.shape[0] != k or (b is not None and b.shape != (n,)):
+        raise ValueError("x [M,K], w [K,N], b [N]")
+    if out is None:
+        out = torch.empty((m, n), dtype=x.dtype, device=x.device)
+    pair = isinstance(out, (tuple, list))
+    y0, y1 = (out[0], out[1]) if pair else (out, None)
+    n0 = y0.shape[1]
+    if y0.shape[0] != m or (y1 is None and n0 != n) or \
+            (y1 is not None and (y1.shape != (m, n - n0))):
+        raise ValueError("out must cover [M, N]")
+    ld0 = _row_stride(y0)
+    ld1 = _row_stride(y1) if y1 is not None else 0
+    with torch.cuda.device(x.device):
+        cabi.call("cfk_linear_fwd", _stream(x.device), _dtype_code(x), _ptr(x), _ptr(w), _ptr(b),
+                  _ptr(y0), ld0, _ptr(y1), ld1, n0, m, k, n)
+    _done(x.device)
+    return out
+
+
+def linear_bwd_dx(dys, ws, out=None):
+    """dx = sum_s dys[s] ws[s]^T (cfk_linear_bwd_dx): dys [M, n_s] (rows may be strided),
+    ws [K, n_s] contiguous; dx [M, K] in their dtype."""
+    if not 1 <= len(dys) == len(ws) <= 4:
+        raise ValueError("1 to 4 (dy, w) blocks")
+    _check(*ws)
+    m = dys[0].shape[0]
+    k = ws[0].shape[0]
+    segs = []
+    for dy, w in zip(dys, ws):
+        if dy.shape[0] != m or w.shape != (k, dy.shape[1]) or dy.dtype != ws[0].dtype:
+            raise ValueError("dy_s [M, n_s] and w_s [K, n_s] of one dtype")
+        segs.append((_ptr(dy), _row_stride(dy), dy.shape[1], _ptr(w), None, None))
+    dx = torch.empty((m, k), dtype=dys[0].dtype, device=dys[0].device) if out is None else out
+    _check(dx)
+    with torch.cuda.device(dx.device):
+        cabi.call("cfk_linear_bwd_dx", _stream(dx.device), _dtype_code(dx),
+                  cabi.linear_segs(*segs), len(segs), _ptr(dx), m, k)
+    _done(dx.device)
+    return dx
+
+
+def linear_bwd_dw(x, dys, with_bias, grads=None, workspace=None):
+    """[(dw_s, db_s)] with dw_s = x^T dys[s] and db_s = the column sums of dys[s] (None where
+    with_bias[s] is false), f32 (cfk_linear_bwd_dw); x [M,K] contiguous is read once.  grads:
+    preallocated [(dw_s, db_s)] or None."""
+    _check(x)
+    m, k = x.shape
+    if not 1 <= len(dys) == len(with_bias) <= 4:
+        raise ValueError("1 to 4 dy blocks")
+    if grads is None:
+        grads = [(torch.empty((k, dy.shape[1]), dtype=torch.float32, device=x.device),
+                  torch.empty(dy.shape[1], dtype=torch.float32, device=x.device) if wb else None)
+                 for dy, wb in zip(dys, with_bias)]
+    segs = []
+    for dy, (dw, db) in zip(dys, grads):
+        _check(dw, db)
+        if dy.shape[0] != m or dw.shape != (k, dy.shape[1]) or dw.dtype != torch.float32:
+            raise ValueError("dy_s [M, n_s], dw_s f32 [K, n_s]")
+        segs.append((_ptr(dy), _row_stride(dy), dy.shape[1], None, _ptr(dw), _ptr(db)))
+    arr = cabi.linear_segs(*segs)
+    with torch.cuda.device(x.device):
+        if workspace is None:
+            nbytes = ctypes.c_size_t(0)
+            cabi.call("cfk_linear_bwd_dw_workspace_size", arr, len(segs), m, k,
+                      ctypes.byref(nbytes))
+            workspace = torch.empty(max(int(nbytes.value), 16), dtype=torch.uint8,
+                                    device=x.device)
+        cabi.call("cfk_linear_bwd_dw", _stream(x.device), _dtype_code(x), _ptr(x), arr,
+                  len(segs), m, k, _ptr(workspace), workspace.numel())
+    _done(x.device)
+    return grads
 
 
 def gate_fwd(g, o, out=None):

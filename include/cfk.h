@@ -213,6 +213,49 @@ CFK_API int cfk_gdp_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, con
                 void* workspace, size_t workspace_bytes, int64_t M, int64_t K, int64_t N);
 
 /* ------------------------------------------------------------------------------------------ */
+/* Plain projections of the attention modules (no counterpart in the reference: the modules  */
+/* that call its kernels do these GEMMs in the host framework).  The forward is the tiling   */
+/* of cuda/volta_ops.cu:143-207 without the gate.                                             */
+/* ------------------------------------------------------------------------------------------ */
+
+/* y = x w + b: x [M,K], w [K,N] row-major, b [N] or NULL, all in dtype, f32 accumulation.
+ * Columns [0, n_split) go to y0 (row stride ld0 elements), columns [n_split, N) to y1 (row
+ * stride ld1; unused when n_split = N), so one call can fill two buffers.  n_split is N or a
+ * multiple of 128 in (0, N).  N % 8 == 0. */
+CFK_API int cfk_linear_fwd(cfk_stream_t stream, cfk_dtype dtype, const void* x, const void* w,
+                   const void* b, void* y0, int64_t ld0, void* y1, int64_t ld1,
+                   int64_t n_split, int64_t M, int64_t K, int64_t N);
+
+/* One column block of a projection's output gradient, for the backward calls below:
+ * dy [M, n] in dtype with row stride ld elements, the block's weight w [K, n] (dtype,
+ * row-major; cfk_linear_bwd_dx), and its f32 gradients dw [K, n] and db [n] (db may be NULL;
+ * cfk_linear_bwd_dw).  n % 8 == 0. */
+typedef struct cfk_linear_seg {
+    const void* dy;
+    int64_t ld;
+    int64_t n;
+    const void* w;
+    float* dw;
+    float* db;
+} cfk_linear_seg;
+
+#define CFK_LINEAR_MAX_SEGS 4
+
+/* dx [M,K] (dtype) = sum over the n_segs (1..4) blocks of dy_s w_s^T, f32 accumulation. */
+CFK_API int cfk_linear_bwd_dx(cfk_stream_t stream, cfk_dtype dtype, const cfk_linear_seg* segs,
+                      int n_segs, void* dx, int64_t M, int64_t K);
+
+/* Bytes of scratch memory cfk_linear_bwd_dw needs for these blocks on the current device. */
+CFK_API int cfk_linear_bwd_dw_workspace_size(const cfk_linear_seg* segs, int n_segs, int64_t M,
+                                     int64_t K, size_t* bytes);
+
+/* dw_s = x^T dy_s and db_s = the column sums of dy_s (f32) for each block, x [M,K] in dtype
+ * read once; deterministic (partial sums over row groups added in a fixed order). */
+CFK_API int cfk_linear_bwd_dw(cfk_stream_t stream, cfk_dtype dtype, const void* x,
+                      const cfk_linear_seg* segs, int n_segs, int64_t M, int64_t K,
+                      void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------------------------------------------------ */
 /* Diagnostics (no counterpart in the reference).                                             */
 /* ------------------------------------------------------------------------------------------ */
 
