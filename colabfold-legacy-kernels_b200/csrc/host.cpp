@@ -56,6 +56,17 @@ int current_device(DeviceInfo* info) {
     if (dev < 0 || dev >= kMaxDevices) {
         return fail(CFK_ERR_UNSUPPORTED_DEVICE, "device ordinal %d out of range", dev);
     }
+    // A thread that never made a runtime call that binds a context (a framework's worker
+    // thread, e.g. an autograd engine's) has none current, and the driver's tensor-map encoder
+    // then fails; cudaSetDevice binds the device's primary context once per thread.
+    thread_local bool bound[kMaxDevices] = {};
+    if (!bound[dev]) {
+        e = cudaSetDevice(dev);
+        if (e != cudaSuccess) {
+            return fail(CFK_ERR_LAUNCH, "cudaSetDevice(%d): %s", dev, cudaGetErrorString(e));
+        }
+        bound[dev] = true;
+    }
     std::call_once(g_dev_once[dev], [dev]() {
         DeviceInfo d;
         d.device = dev;

@@ -10,19 +10,23 @@ attention (AlphaFold 2 supplement, Algorithms 13 and 14):
 This module runs that composition forward and backward on a B200:
 
 * LayerNorm forward/backward: cfk_ln_fwd / cfk_ln_bwd.
-* The projections: one GEMM x [Wq|Wk|Wv] into a [Ni, Nj, 3, H, D] buffer, one for the bias and
-  one for the gate (cuBLAS through torch, bf16 with f32 accumulation).
+* The projections on this build's tcgen05 kernels (cfk_linear_*): one launch x [Wq|Wk|Wv|Wg]
+  + [0|0|0|bg] writes q|k|v into a [Ni, Nj, 3, H, D] buffer and the gate pre-activation into
+  its own; the pair bias x Wb (Wb zero-padded to 16 columns) is a second small launch.  Their
+  backward is one cfk_linear_bwd_dx over the blocks (dq|dk|dv, dg, the bias rows) and one
+  cfk_linear_bwd_dw that reads x once (f32 weight and bias gradients, fixed summation order).
 * Attention forward/backward: cfk_attn_fwd_strided / cfk_attn_bwd_strided.  q, k, v are views
   of the projection buffer and the output is written straight into [Ni, Nj, H, D] storage, for
   attention along either axis (around the ending node, or along an MSA column, the batch axis
   is the second axis, which is just other strides), so no transposed copy of q, k, v, o or of
   their gradients is made; dq, dk and dv land in views of one [Ni, Nj, 3, H, D] gradient
   buffer that feeds the projection's weight gradient directly.
-* The gate: cfk_gate_fwd / cfk_gate_bwd, one fused pass each way; the output projection: a
-  cuBLAS GEMM.
+* The gate: cfk_gate_fwd / cfk_gate_bwd, one fused pass each way; the output projection:
+  cfk_linear_fwd, cfk_linear_bwd_dx and cfk_linear_bwd_dw.
 
-Activations are bf16; LayerNorm's gamma and beta are f32 (the kernels' contract); the weights are
-kept in f32 and cast to bf16 for the GEMMs, so their gradients arrive in f32.
+No cuBLAS GEMM runs in a module step.  Activations are bf16; LayerNorm's gamma and beta are f32
+(the kernels' contract); the weights are f32 master copies cast to bf16 for the kernels, and
+their gradients come back in f32 straight from the f32 tensor-memory accumulators.
 """
 
 import math
@@ -49,25 +53,102 @@ class _LayerNorm(torch.autograd.Function):
 
 
 class _Linear(torch.autograd.Function):
-    """y = x W (+ b) whose bias gradient is a GEMV (dy^T 1) rather than a column reduction of
-    dy, which for [590k, 128] bf16 gradients is several times slower."""
+    """y = x W + b on this build's kernels (cfk_linear_fwd / cfk_linear_bwd_dx /
+    cfk_linear_bwd_dw); W [K, N] and b [N] are f32 master weights cast to x's dtype for the
+    kernels, and their gradients are returned in f32."""
 
     @staticmethod
     def forward(ctx, x, w, b):
-        ctx.save_for_backward(x, w)
+        w16 = w.to(x.dtype).contiguous()
+        y = torch_ops.linear_fwd(x, w16, b.to(x.dtype) if b is not None else None)
+        ctx.save_for_backward(x, w16)
         ctx.has_bias = b is not None
-        return torch.addmm(b, x, w) if b is not None else x @ w
+        return y
 
     @staticmethod
     def backward(ctx, dy):
-        x, w = ctx.saved_tensors
-        dx = dy @ w.t() if ctx.needs_input_grad[0] else None
-        dw = x.t() @ dy if ctx.needs_input_grad[1] else None
-        db = None
-        if ctx.has_bias and ctx.needs_input_grad[2]:
-            ones = torch.ones(dy.shape[0], 1, dtype=dy.dtype, device=dy.device)
-            db = (dy.t() @ ones).view(-1)
+        x, w16 = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = torch_ops.linear_bwd_dx([dy], [w16]) if ctx.needs_input_grad[0] else None
+        (dw, db), = torch_ops.linear_bwd_dw(x, [dy], [ctx.has_bias])
         return dx, dw, db
+
+
+def _pad16(w, dtype):
+    """w [C, n] (n <= 16) zero-padded to [C, 16] in dtype: the kernels take column blocks that
+    are multiples of 8 (16 for the dx pass), and a pair bias has H = 4 or 8 columns."""
+    out = torch.zeros((w.shape[0], 16), dtype=dtype, device=w.device)
+    out[:, :w.shape[1]] = w.to(dtype)
+    return out
+
+
+class _PairBias(torch.autograd.Function):
+    """x W_b [M, H] (no bias term), through a 16-column padded weight."""
+
+    @staticmethod
+    def forward(ctx, x, w_b):
+        wb16 = _pad16(w_b, x.dtype)
+        y = torch_ops.linear_fwd(x, wb16)
+        ctx.save_for_backward(x, wb16)
+        ctx.h = w_b.shape[1]
+        return y[:, :ctx.h]
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, wb16 = ctx.saved_tensors
+        d16 = torch.zeros((x.shape[0], 16), dtype=x.dtype, device=x.device)
+        d16[:, :ctx.h] = dy
+        dx = torch_ops.linear_bwd_dx([d16], [wb16]) if ctx.needs_input_grad[0] else None
+        (dw, _), = torch_ops.linear_bwd_dw(x, [d16], [False])
+        return dx, dw[:, :ctx.h]
+
+
+class _InProj(torch.autograd.Function):
+    """The input projections of a gated attention from x [M, C]: qkv [M, 3HD] = x [Wq|Wk|Wv],
+    g [M, HD] = x Wg + bg, and, when w_b is given (triangle attention), the pair-bias rows
+    [M, 16] = x Wb (zero-padded; columns [0, H) are the bias).  The forward writes q|k|v and g
+    into their own buffers from one cfk_linear_fwd (two where 3HD is not a multiple of 128);
+    the backward is one cfk_linear_bwd_dx over the blocks dq|dk|dv, dg (and the bias rows) and
+    one cfk_linear_bwd_dw, which reads x once."""
+
+    @staticmethod
+    def forward(ctx, x, w_qkv, w_g, b_g, w_b):
+        dt, m = x.dtype, x.shape[0]
+        hd3, hd = w_qkv.shape[1], w_g.shape[1]
+        w_all = torch.cat([w_qkv, w_g], 1).to(dt).contiguous()
+        qkv = torch.empty((m, hd3), dtype=dt, device=x.device)
+        g = torch.empty((m, hd), dtype=dt, device=x.device)
+        if hd3 % 128 == 0:
+            b_all = torch.cat([torch.zeros(hd3, device=x.device), b_g]).to(dt)
+            torch_ops.linear_fwd(x, w_all, b_all, out=(qkv, g))
+        else:
+            torch_ops.linear_fwd(x, w_all[:, :hd3].contiguous(), None, out=qkv)
+            torch_ops.linear_fwd(x, w_all[:, hd3:].contiguous(), b_g.to(dt), out=g)
+        if w_b is not None:
+            wb16 = _pad16(w_b, dt)
+            b16 = torch_ops.linear_fwd(x, wb16)
+        else:
+            wb16 = b16 = x.new_empty(0)
+        ctx.save_for_backward(x, w_all, wb16)
+        ctx.hd3 = hd3
+        ctx.nb = w_b.shape[1] if w_b is not None else 0
+        return qkv, g, b16
+
+    @staticmethod
+    def backward(ctx, d_qkv, d_g, d_b16):
+        x, w_all, wb16 = ctx.saved_tensors
+        hd3 = ctx.hd3
+        dys = [d_qkv.contiguous(), d_g.contiguous()]
+        ws = [w_all[:, :hd3].contiguous(), w_all[:, hd3:].contiguous()]
+        with_bias = [False, True]
+        if ctx.nb:
+            dys.append(d_b16.contiguous())
+            ws.append(wb16)
+            with_bias.append(False)
+        dx = torch_ops.linear_bwd_dx(dys, ws) if ctx.needs_input_grad[0] else None
+        grads = torch_ops.linear_bwd_dw(x, dys, with_bias)
+        d_wb = grads[2][0][:, :ctx.nb] if ctx.nb else None
+        return dx, grads[0][0], grads[1][0], grads[1][1], d_wb
 
 
 class _Gate(torch.autograd.Function):
@@ -121,17 +202,19 @@ class _Attention(torch.autograd.Function):
 
 
 def _gated_attention(x, a, b, heads, head_dim, w_qkv, w_g, b_g, w_o, b_o, bias, kmask,
-                     over_first):
+                     over_first, w_b=None, bias_view=None):
     """Gated attention over one axis of normalised rows x [a*b, C] (bf16) laid out [a, b, C]:
     over the second axis (batch = first axis) or, with over_first, over the first (batch =
-    second axis).  bias [H, S, S] bf16 (S = the attended axis' length), kmask u8 [batch, S].
+    second axis).  bias [H, S, S] bf16 (S = the attended axis' length), or, with w_b, the pair
+    bias x Wb reshaped by bias_view(rows [a*b, H]) -> [H, S, S].  kmask u8 [batch, S].
     Returns [a*b, C_out]."""
-    bf = torch.bfloat16
-    qkv = _Linear.apply(x, w_qkv.to(bf), None).view(a, b, 3, heads, head_dim)
-    o = _Attention.apply(qkv, bias, kmask, 1.0 / math.sqrt(head_dim), over_first)
-    g = _Linear.apply(x, w_g.to(bf), b_g.to(bf))
+    qkv, g, b16 = _InProj.apply(x, w_qkv, w_g, b_g, w_b)
+    if w_b is not None:
+        bias = bias_view(b16[:, :w_b.shape[1]])
+    o = _Attention.apply(qkv.view(a, b, 3, heads, head_dim), bias, kmask,
+                         1.0 / math.sqrt(head_dim), over_first)
     gated = _Gate.apply(g, o.view(a * b, heads * head_dim))
-    return _Linear.apply(gated, w_o.to(bf), b_o.to(bf))
+    return _Linear.apply(gated, w_o, b_o)
 
 
 class _GatedAttentionParams(torch.nn.Module):
@@ -159,10 +242,10 @@ class _GatedAttentionParams(torch.nn.Module):
         return _LayerNorm.apply(t.to(torch.bfloat16).reshape(a * b, c), self.gamma, self.beta,
                                 self.eps)
 
-    def _attend(self, x, a, b, bias, kmask, over_first):
+    def _attend(self, x, a, b, bias, kmask, over_first, w_b=None, bias_view=None):
         w_qkv = torch.cat([self.w_q, self.w_k, self.w_v], dim=1)
         return _gated_attention(x, a, b, self.heads, self.head_dim, w_qkv, self.w_g, self.b_g,
-                                self.w_o, self.b_o, bias, kmask, over_first)
+                                self.w_o, self.b_o, bias, kmask, over_first, w_b, bias_view)
 
 
 class TriangleAttention(_GatedAttentionParams):
@@ -183,13 +266,16 @@ class TriangleAttention(_GatedAttentionParams):
         if ni != nj or mask.shape != (ni, nj):
             raise ValueError("triangle attention needs a square pair representation and mask")
         x = self._norm(z)
-        b = _Linear.apply(x, self.w_b.to(torch.bfloat16), None).view(ni, nj, self.heads)
-        # bias[h, query, key]: (x Wb)[query, key] around the starting node, [key, query] around
-        # the ending node (the pair swapped with the residue axes)
-        bias = b.permute(2, 1, 0) if ending else b.permute(2, 0, 1)
+
+        def bias_view(rows):
+            # bias[h, query, key]: (x Wb)[query, key] around the starting node, [key, query]
+            # around the ending node (the pair swapped with the residue axes)
+            b = rows.view(ni, nj, self.heads)
+            return b.permute(2, 1, 0) if ending else b.permute(2, 0, 1)
+
         keep = (mask != 0).to(torch.uint8)
         kmask = (keep.t() if ending else keep).contiguous()
-        return self._attend(x, ni, nj, bias, kmask, ending).view(ni, nj, c)
+        return self._attend(x, ni, nj, None, kmask, ending, self.w_b, bias_view).view(ni, nj, c)
 
 
 class MSARowAttentionWithPairBias(_GatedAttentionParams):
@@ -214,7 +300,7 @@ class MSARowAttentionWithPairBias(_GatedAttentionParams):
         x = self._norm(m)
         zn = _LayerNorm.apply(z.to(torch.bfloat16).reshape(r * r, z.shape[2]), self.gamma_z,
                               self.beta_z, self.eps)
-        bias = _Linear.apply(zn, self.w_b.to(torch.bfloat16), None).view(r, r, self.heads)
+        bias = _PairBias.apply(zn, self.w_b).view(r, r, self.heads)
         kmask = (msa_mask != 0).to(torch.uint8).contiguous()
         return self._attend(x, s, r, bias.permute(2, 0, 1), kmask, False).view(s, r, c)
 

@@ -1,6 +1,7 @@
 """The triangle-attention module on the GPU (colabfold_legacy_kernels.modules.TriangleAttention:
-LayerNorm, attention through strided views, cuBLAS projections) against the float64 oracle of
-config C1's module (oracle/module.py), forward and backward, around both nodes.
+LayerNorm, attention through strided views, projections on the cfk_linear_* kernels) against
+the float64 oracle of config C1's module (oracle/module.py), forward and backward, around both
+nodes; and that a module step launches no library GEMM.
 
 Tolerances: the output, elementwise atol = rtol = 2e-2 (bf16).  Gradients of z and of every
 parameter are sums over all 16384 pair rows of products of bf16 values, so they are held to a
@@ -85,6 +86,41 @@ def test_module_makes_no_transposed_copies(cuda_device):
     torch.cuda.synchronize()
     assert calls.count("cfk_attn_fwd_strided") == 2 and calls.count("cfk_attn_bwd_strided") == 2
     assert "cfk_attn_fwd" not in calls and "cfk_attn_bwd" not in calls
+
+
+def test_module_step_launches_no_library_gemm(cuda_device):
+    """Forward and backward of the triangle module (both nodes) run their projections on this
+    build's kernels: the profiler's CUDA kernel list holds no cuBLAS / CUTLASS GEMM or GEMV,
+    and the C ABI saw the projection entry points."""
+    import re
+    from colabfold_legacy_kernels import cabi
+    z, mask, p = _case(seed=3, n=64, padded=True)
+    m = _module(p)
+    calls = []
+    real = cabi.call
+
+    def spy(name, *args):
+        calls.append(name)
+        return real(name, *args)
+
+    cabi.call = spy
+    try:
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            for ending in (False, True):
+                zg = z.cuda().requires_grad_(True)
+                m(zg, mask.cuda(), ending=ending).float().sum().backward()
+            torch.cuda.synchronize()
+    finally:
+        cabi.call = real
+    names = {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
+    library = sorted(n for n in names
+                     if re.search(r"gemm|gemv|nvjet|xmma|cublas|cutlass", n, re.IGNORECASE))
+    assert not library, "library GEMM kernels in a module step: %s" % library[:5]
+    assert any("gdp_fwd_kernel" in n for n in names)
+    assert any("linear_dx_kernel" in n for n in names)
+    assert any("linear_dw_kernel" in n for n in names)
+    for fn in ("cfk_linear_fwd", "cfk_linear_bwd_dx", "cfk_linear_bwd_dw"):
+        assert fn in calls, fn
 
 
 def _msa_case(column, seed):
