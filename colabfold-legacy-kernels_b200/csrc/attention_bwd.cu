@@ -12,8 +12,11 @@
 // each chunk writes its own partial tile and a second launch adds the chunks in a fixed
 // order, so the result does not depend on scheduling).  dQ, dK and dV of one batch row are then
 // partial sums over key tiles (dQ) or query tiles (dK, dV); the MMA writes those partials into
-// tensor memory and a TMA tensor reduce-add folds them into f32 accumulators in the workspace.
-// A final kernel converts the accumulators to 16 bits.
+// tensor memory.  Head dims 8-32: the drain rounds each partial to the output's 16-bit type and
+// a TMA tensor reduce-add adds it straight into dQ, dK, dV (zeroed first; the reduce rounds
+// once per add, 6 adds at S = 768), which halves the bytes the L2 reduces -- the bound of this
+// kernel -- against f32 accumulators, and needs no conversion pass.  Head dim 64 keeps f32
+// accumulators in the workspace and a final conversion kernel.
 //
 // The scores are computed transposed, S^T = K Q^T and dP^T = V dO^T, so that a thread owns one
 // key row j of the tile and writes P^T and dS^T rows straight into tensor memory, where they
@@ -34,12 +37,13 @@
 // weight exp(-1e4 - lse) underflows, i.e. for every query tile whose rows all have
 // lse > -9900; the prep kernel flags the other tiles (rows with every key masked, or biases
 // below -1e4), and those take an exact path that evaluates the masked logit -1e4 per key.
-// dS is kept unscaled; the conversion multiplies dQ and dK by the softmax scale.
+// dS is kept unscaled; the drain multiplies the dQ and dK partials by the softmax scale.
 //
 //   warps 0-15   dS warps: warp w4 + 4w owns key rows [32 w4, +32) (its tensor-memory lane
 //                quarter) and query columns [32w, +32) of warpgroup w.
 //   warps 16-19  drain warpgroup: the dV, dK and dQ partials of each step, tensor memory ->
-//                swizzled staging -> TMA reduce-add, beside the dS warps' next step.
+//                16-bit swizzled staging -> TMA reduce-add into the outputs, beside the dS
+//                warps' next step.
 //   warp 20      TMA producer: per batch row q, dO, k, v tiles, the query tile's statistics
 //                block, and the key-mask operand rows it writes itself.
 //   warp 21      MMA issuer (warps 22, 23 idle: they complete the last warpgroup, which
@@ -64,8 +68,9 @@ struct BwdParams {
     const uint8_t* stats;  // kStatBytes per (batch row, head, query tile)
     float* dbias_out;      // dbias, or the first batch chunk's partial tile set
     int64_t dbias_stride;  // floats between the partials of consecutive batch chunks (0: one)
-    int dbias_accumulate;  // add this launch's sums to dbias_out (rows of earlier launches)
-    int b_base, b_end;     // the batch rows of this launch (the accumulators hold b - b_base)
+    int dbias_accumulate;  // add this launch's sums to dbias_out instead of storing them
+    int b_base, b_end;     // the batch rows of this launch (head dim 64's accumulators hold
+                           // rows b - b_base)
     int N, H, Sq, Sk;
     int n_it, n_jt, n_bc, bchunk;
     int64_t items;
@@ -160,11 +165,10 @@ struct BwdCfg {
     static constexpr int kOffAS = kOffStat + ((kStatBytes + 127) / 128) * 128; // key-mask rows
     static constexpr int kStageBytes = ((kOffAS + 2048 + 1023) / 1024) * 1024;
 
-    // f32 staging of one [128 x D] partial for the TMA reduce: panels of kPW floats per row
-    static constexpr int kPW = D < 32 ? D : 32;
-    static constexpr int kRowB = kPW * 4; // bytes of one staging row (= swizzle span)
-    static constexpr int kPanelBytes = 128 * kRowB;
-    static constexpr int kStgBytes = 128 * D * 4;
+    // 16-bit staging of one [128 x D] partial for the TMA reduce (rows of 2D bytes, the
+    // swizzle span of the output maps)
+    static constexpr int kRowB = 2 * D;
+    static constexpr int kStgBytes = 128 * kRowB;
 
     static constexpr int kOffStages = 0;
     static constexpr int kOffDS = NST * kStageBytes;    // dS^T rows, MN-major operand of dQ
@@ -202,9 +206,9 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_do,
-                    const __grid_constant__ CUtensorMap tm_dq_acc,
-                    const __grid_constant__ CUtensorMap tm_dk_acc,
-                    const __grid_constant__ CUtensorMap tm_dv_acc, const BwdParams p) {
+                    const __grid_constant__ CUtensorMap tm_dq,
+                    const __grid_constant__ CUtensorMap tm_dk,
+                    const __grid_constant__ CUtensorMap tm_dv, const BwdParams p) {
     using C = BwdCfg<D>;
     using G = Geo<D>;
     using E = Elem<T>;
@@ -421,9 +425,9 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     } else if (wgrp == 4) {
         // =============================== drain warpgroup ===============================
         // Partial sums of step g: tensor memory -> registers (the buffer is released after the
-        // third) -> swizzled staging (two buffers, alternating) -> TMA reduce-add into the f32
-        // accumulators (dV, dK at key rows, dQ at query rows).  Every thread reaches every named
-        // barrier of a step, also when a wait gave up.
+        // third) -> 16-bit, dK and dQ times the softmax scale -> swizzled staging (two buffers,
+        // alternating) -> TMA reduce-add into dV, dK (key rows) and dQ (query rows) of batch
+        // row b.  Every thread reaches every named barrier of a step, also when a wait gave up.
         setmaxnreg_dec<C::kOtherRegs>();
         const int dw = warp - C::kDrainWarp0;
         const int row = 32 * dw + lane;
@@ -443,7 +447,6 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
                 }
                 __syncwarp();
                 tc_fence_after();
-                const int bh = (b - p.b_base) * p.H + w.h; // accumulator rows of this launch
 #pragma unroll 1
                 for (int pp = 0; pp < 3; ++pp) {
                     const uint32_t stg = sbase + C::kOffStg + (pc & 1) * C::kStgBytes;
@@ -469,25 +472,24 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
                                 mbar_arrive(part_empty);
                             }
                         }
+                        const float mul = pp == 0 ? 1.f : p.scale;
 #pragma unroll
-                        for (int q = 0; q < kHalf / 4; ++q) {
-                            const int col = h0 + q * 4;
-                            sts128(stg + (col / C::kPW) * C::kPanelBytes +
-                                       stg_chunk<C::kRowB>(row, (col % C::kPW) / 4),
-                                   make_uint4(raw[4 * q], raw[4 * q + 1], raw[4 * q + 2],
-                                              raw[4 * q + 3]));
+                        for (int q = 0; q < kHalf / 8; ++q) {
+                            uint32_t o[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                o[e] = E::pack(__uint_as_float(raw[8 * q + 2 * e]) * mul,
+                                               __uint_as_float(raw[8 * q + 2 * e + 1]) * mul);
+                            }
+                            sts128(stg + stg_chunk<C::kRowB>(row, (h0 + 8 * q) / 8),
+                                   make_uint4(o[0], o[1], o[2], o[3]));
                         }
                     }
                     fence_proxy_async_smem();
                     named_bar_sync(1, 128);
                     if (leader) {
-                        const CUtensorMap* tm = pp == 0 ? &tm_dv_acc : (pp == 1 ? &tm_dk_acc : &tm_dq_acc);
-                        const int row0 = pp == 2 ? i0 : j0;
-#pragma unroll
-                        for (int pn = 0; pn < D / C::kPW; ++pn) {
-                            tma_reduce_add_3d(tm, smem + (stg - sbase) + pn * C::kPanelBytes,
-                                              pn * C::kPW, row0, bh);
-                        }
+                        const CUtensorMap* tm = pp == 0 ? &tm_dv : (pp == 1 ? &tm_dk : &tm_dq);
+                        tma_reduce_add_4d(tm, smem + (stg - sbase), 0, pp == 2 ? i0 : j0, w.h, b);
                         bulk_commit();
                     }
                     ++pc;
@@ -1296,12 +1298,6 @@ constexpr size_t align256(size_t x) {
 // SM count of every compute capability 10.0 part).
 constexpr int kWorkspaceSms = 160;
 
-// f32 accumulator bytes one launch of the main kernel may use; larger problems are processed in
-// ranges of batch rows, one launch each, which bounds the workspace.  (Ranges small enough for
-// the accumulators to stay in the 126 MB L2 were measured slower at tri-768: 3.37 against
-// 2.85 ms per step, the per-launch pipeline fill and drain outweighing the L2-resident
-// reductions.)
-constexpr int64_t kRangeAccBytes = 4ll << 30;
 
 // Batch chunks of a launch with `base` (head, query tile, key tile) items: as many as fit in
 // one wave of `sms` CTAs, at least one, at most the launch's rows.
@@ -1313,37 +1309,19 @@ int64_t batch_chunks(int64_t rows, int64_t base, int64_t sms) {
     return std::min<int64_t>(nbc, rows);
 }
 
-// Batch rows per launch of the main kernel (head dim 64 keeps all rows in one launch).  The
-// accumulator budget can be lowered through $CFK_BWD_RANGE_BYTES (tests use it to exercise
-// several ranges on small problems).
-int64_t range_rows(int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D) {
-    const int64_t row_bytes = 4 * H * (Sq + 2 * Sk) * D;
-    if (D == 64 || row_bytes <= 0) {
-        return std::max<int64_t>(N, 1);
-    }
-    int64_t budget = kRangeAccBytes;
-    if (const char* env = std::getenv("CFK_BWD_RANGE_BYTES")) {
-        const long long v = std::atoll(env);
-        if (v > 0) {
-            budget = v;
-        }
-    }
-    const int64_t r = std::max<int64_t>(1, budget / row_bytes);
-    // one launch when the split would buy little
-    return N <= r + r / 2 ? std::max<int64_t>(N, 1) : r;
-}
-
+// Workspace of the backward: f32 dq, dk, dv accumulators (head dim 64 only; the other head dims
+// reduce straight into the outputs), the row statistics blocks and, when the batch rows are
+// split into chunks, the chunks' dbias partials.
 struct BwdWorkspace {
     size_t dq_off, dk_off, dv_off, stat_off, dbp_off, total;
-    int64_t range;       // batch rows per launch of the main kernel
-    int64_t max_chunks;  // batch chunks (dbias partials) of one launch at most
+    int64_t max_chunks;  // batch chunks (dbias partials) of the launch at most
 };
 
 BwdWorkspace bwd_workspace(int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D) {
     BwdWorkspace w;
-    w.range = std::min<int64_t>(range_rows(N, H, Sq, Sk, D), std::max<int64_t>(N, 1));
-    const size_t eq = static_cast<size_t>(w.range * H * Sq * D) * 4;
-    const size_t ekv = static_cast<size_t>(w.range * H * Sk * D) * 4;
+    const int64_t acc_rows = D == 64 ? N : 0;
+    const size_t eq = static_cast<size_t>(acc_rows * H * Sq * D) * 4;
+    const size_t ekv = static_cast<size_t>(acc_rows * H * Sk * D) * 4;
     const int64_t n_it = (Sq + kBM - 1) / kBM;
     const int64_t n_jt = (Sk + kBN - 1) / kBN;
     w.dq_off = 0;
@@ -1352,19 +1330,21 @@ BwdWorkspace bwd_workspace(int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t
     w.stat_off = w.dv_off + align256(ekv);
     w.dbp_off = w.stat_off + align256(static_cast<size_t>(N * H * n_it) * kStatBytes);
     // batch rows per chunk -> number of chunks, as the launch computes it
-    const int64_t nbc = batch_chunks(w.range, H * n_it * n_jt, kWorkspaceSms);
-    const int64_t bchunk = (w.range + nbc - 1) / std::max<int64_t>(nbc, 1);
-    w.max_chunks = bchunk > 0 ? (w.range + bchunk - 1) / bchunk : 1;
+    const int64_t rows = std::max<int64_t>(N, 1);
+    const int64_t nbc = batch_chunks(rows, H * n_it * n_jt, kWorkspaceSms);
+    const int64_t bchunk = (rows + nbc - 1) / std::max<int64_t>(nbc, 1);
+    w.max_chunks = bchunk > 0 ? (rows + bchunk - 1) / bchunk : 1;
     w.total = w.dbp_off + (w.max_chunks > 1 ? align256(static_cast<size_t>(w.max_chunks * H * Sq *
                                                                           Sk) * 4)
                                             : 0);
     return w;
 }
 
-// Phase 0 (bit 1): row statistics of every row.  Phase 1 (bit 2): per range of batch rows,
-// zero the accumulators, run the main kernel and convert the range's dq, dk, dv -- except the
-// last range's conversion, which is phase 2 (bit 4); dbias is final after phase 1, so a
-// caller can reduce it across GPUs while phase 2 runs.
+// Phase 0 (bit 1): row statistics of every row.  Phase 1 (bit 2): zero dq, dk, dv (head dims
+// 8-32: the main kernel adds its 16-bit partials straight into them) or the f32 accumulators
+// (head dim 64), run the main kernel and add dbias's batch chunks.  Phase 2 (bit 4): head dim
+// 64 converts its accumulators to 16 bits; nothing for the others.  dbias is final after
+// phase 1, so a caller can reduce it across GPUs while phase 2 runs.
 template <typename T, int D>
 int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                const void* v, const void* bias, const uint8_t* kmask, const void* out,
@@ -1393,37 +1373,28 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
     p.scale = scale;
     p.mask_bits = mask_bias_bits(scale);
     const int64_t base = static_cast<int64_t>(H) * p.n_it * p.n_jt;
+    const int64_t nh = static_cast<int64_t>(N) * H;
 
     if (phases & 1) {
-        const int64_t nh = static_cast<int64_t>(N) * H;
         attn_bwd_prep_kernel<T, D><<<static_cast<unsigned>(nh * p.n_it), 128, 0, st>>>(
             static_cast<const T*>(out), static_cast<const T*>(dout), lse, stats, Sq, p.n_it, scale,
             kInplace ? 0u : p.mask_bits, row_strides(views[3], D), row_strides(views[4], D));
         CFK_TRY(check_launch("attn_bwd_prep"));
     }
-    if (!(phases & 6)) {
-        return CFK_OK;
-    }
-    CUtensorMap tq, tk, tv, tdo;
+    const int64_t rq = nh * Sq * D / 8;
+    const int64_t rkv = nh * Sk * D / 8;
+    const RowStrides out_views[3] = {row_strides(views[5], D), row_strides(views[6], D),
+                                     row_strides(views[7], D)};
     if (phases & 2) {
+        CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
         CFK_TRY(make_tmap_rows(&tq, q, views[0], D, kBM, G::kSwizzleBytes, "bwd q"));
         CFK_TRY(make_tmap_rows(&tk, k, views[1], D, kBN, G::kSwizzleBytes, "bwd k"));
         CFK_TRY(make_tmap_rows(&tv, v, views[2], D, kBN, G::kSwizzleBytes, "bwd v"));
         CFK_TRY(make_tmap_rows(&tdo, dout, views[4], D, kBM, G::kSwizzleBytes, "bwd dout"));
-    }
-    const int64_t n_ranges = (N + wl.range - 1) / wl.range;
-    // the first design's dS carries the softmax scale; the second's is unscaled
-    const float mqk = kInplace ? 1.f : scale;
-    for (int64_t rg = 0; rg < n_ranges; ++rg) {
-        const int b0 = static_cast<int>(rg * wl.range);
-        const int nr = static_cast<int>(std::min<int64_t>(wl.range, N - b0));
-        const int64_t nh = static_cast<int64_t>(nr) * H;
-        const bool last = rg + 1 == n_ranges;
-        if (phases & 2) {
+        if constexpr (kInplace) {
             if (cudaMemsetAsync(ws, 0, wl.stat_off, st) != cudaSuccess) {
                 return fail(CFK_ERR_LAUNCH, "cfk_attn_bwd: memset failed");
             }
-            CUtensorMap tdq, tdk, tdv;
             const uint64_t frow = 4ull * D;
             CFK_TRY(make_tmap_3d(&tdq, dq_acc, D, Sq, nh, frow, frow * Sq, C::kPW, kBM, 1,
                                  C::kRowB, "bwd dq acc", true));
@@ -1431,50 +1402,61 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
                                  C::kRowB, "bwd dk acc", true));
             CFK_TRY(make_tmap_3d(&tdv, dv_acc, D, Sk, nh, frow, frow * Sk, C::kPW, kBN, 1,
                                  C::kRowB, "bwd dv acc", true));
-            // batch chunks: as many as fit in one wave of CTAs, within what the workspace holds
-            const int64_t nbc = std::min(batch_chunks(nr, base, dev.num_sms), wl.max_chunks);
-            p.bchunk = static_cast<int>((nr + nbc - 1) / nbc);
-            p.n_bc = static_cast<int>((nr + p.bchunk - 1) / p.bchunk);
-            p.items = base * p.n_bc;
-            p.b_base = b0;
-            p.b_end = b0 + nr;
-            const bool chunked = p.n_bc > 1;
-            p.dbias_out = chunked ? reinterpret_cast<float*>(ws + wl.dbp_off) : dbias;
-            p.dbias_stride = chunked ? static_cast<int64_t>(H) * Sq * Sk : 0;
-            p.dbias_accumulate = (!chunked && rg > 0) ? 1 : 0;
-            auto kern = kInplace ? attn_bwd_inplace_kernel<T, 64>
-                                 : attn_bwd_kernel<T, (D < 64 ? D : 32)>;
-            CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device,
-                                     C::kSmemBytes, "attn_bwd",
-                                     kInplace ? 0 : BwdCfg<(D < 64 ? D : 32)>::kLaunchRegs));
-            const int grid = static_cast<int>(std::min<int64_t>(p.items, dev.num_sms));
-            kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, tdq, tdk, tdv, p);
-            CFK_TRY(check_launch("attn_bwd"));
-            if (chunked) {
-                const int64_t n = static_cast<int64_t>(H) * Sq * Sk;
-                const int blocks =
-                    static_cast<int>(std::min<int64_t>((n + 255) / 256, dev.num_sms * 8));
-                dbias_chunks_kernel<<<blocks, 256, 0, st>>>(p.dbias_out, dbias, n, p.n_bc,
-                                                            rg > 0 ? 1 : 0);
-                CFK_TRY(check_launch("attn_bwd dbias chunks"));
-            }
+        } else {
+            // the outputs themselves (views allowed), zeroed first
+            const ConvertJob zero{{nullptr, nullptr, nullptr},
+                                  {dq, dk, dv},
+                                  {rq, rkv, rkv},
+                                  {out_views[0], out_views[1], out_views[2]},
+                                  {1.f, 1.f, 1.f},
+                                  {0, 0, 0},
+                                  d8_log2(D)};
+            f32_to_16_kernel<T><<<dev.num_sms * 8, 256, 0, st>>>(zero);
+            CFK_TRY(check_launch("attn_bwd zero"));
+            // the maps the reduce-adds go through declare the float type (the add is a float add)
+            constexpr Map16 kRed = Elem<T>::kBf16 ? Map16::kBF16 : Map16::kF16;
+            CFK_TRY(make_tmap_rows(&tdq, dq, views[5], D, kBM, G::kSwizzleBytes, "bwd dq", kRed));
+            CFK_TRY(make_tmap_rows(&tdk, dk, views[6], D, kBN, G::kSwizzleBytes, "bwd dk", kRed));
+            CFK_TRY(make_tmap_rows(&tdv, dv, views[7], D, kBN, G::kSwizzleBytes, "bwd dv", kRed));
         }
-        // the range's conversion: in phase 1, or for the last range in phase 2
-        if ((last && (phases & 4)) || (!last && (phases & 2))) {
-            const int64_t rq = nh * Sq * D / 8;
-            const int64_t rkv = nh * Sk * D / 8;
-            const int64_t r0 = static_cast<int64_t>(b0) * H;
-            const ConvertJob job{{dq_acc, dk_acc, dv_acc},
-                                 {dq, dk, dv},
-                                 {rq, rkv, rkv},
-                                 {row_strides(views[5], D), row_strides(views[6], D),
-                                  row_strides(views[7], D)},
-                                 {mqk, mqk, 1.f},
-                                 {r0 * Sq, r0 * Sk, r0 * Sk},
-                                 d8_log2(D)};
-            f32_to_16_kernel<T><<<dev.num_sms * 8, 256, 0, st>>>(job);
-            CFK_TRY(check_launch("attn_bwd convert"));
+        // batch chunks: as many as fit in one wave of CTAs, within what the workspace holds
+        const int64_t nbc = std::min(batch_chunks(N, base, dev.num_sms), wl.max_chunks);
+        p.bchunk = static_cast<int>((N + nbc - 1) / nbc);
+        p.n_bc = static_cast<int>((N + p.bchunk - 1) / p.bchunk);
+        p.items = base * p.n_bc;
+        p.b_base = 0;
+        p.b_end = N;
+        const bool chunked = p.n_bc > 1;
+        p.dbias_out = chunked ? reinterpret_cast<float*>(ws + wl.dbp_off) : dbias;
+        p.dbias_stride = chunked ? static_cast<int64_t>(H) * Sq * Sk : 0;
+        p.dbias_accumulate = 0;
+        auto kern = kInplace ? attn_bwd_inplace_kernel<T, 64>
+                             : attn_bwd_kernel<T, (D < 64 ? D : 32)>;
+        CFK_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), dev.device, C::kSmemBytes,
+                                 "attn_bwd",
+                                 kInplace ? 0 : BwdCfg<(D < 64 ? D : 32)>::kLaunchRegs));
+        const int grid = static_cast<int>(std::min<int64_t>(p.items, dev.num_sms));
+        kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, tdq, tdk, tdv, p);
+        CFK_TRY(check_launch("attn_bwd"));
+        if (chunked) {
+            const int64_t n = static_cast<int64_t>(H) * Sq * Sk;
+            const int blocks =
+                static_cast<int>(std::min<int64_t>((n + 255) / 256, dev.num_sms * 8));
+            dbias_chunks_kernel<<<blocks, 256, 0, st>>>(p.dbias_out, dbias, n, p.n_bc, 0);
+            CFK_TRY(check_launch("attn_bwd dbias chunks"));
         }
+    }
+    if (kInplace && (phases & 4)) {
+        // the first design's dS carries the softmax scale: no multiplier here
+        const ConvertJob job{{dq_acc, dk_acc, dv_acc},
+                             {dq, dk, dv},
+                             {rq, rkv, rkv},
+                             {out_views[0], out_views[1], out_views[2]},
+                             {1.f, 1.f, 1.f},
+                             {0, 0, 0},
+                             d8_log2(D)};
+        f32_to_16_kernel<T><<<dev.num_sms * 8, 256, 0, st>>>(job);
+        CFK_TRY(check_launch("attn_bwd convert"));
     }
     return CFK_OK;
 }

@@ -136,7 +136,7 @@ namespace {
 // cuTensorMapEncodeTiled of a rank-3 or rank-4 map (dim 0 contiguous)
 int encode_tiled(CUtensorMap* map, int rank, const void* base, const uint64_t* dims,
                  const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes,
-                 const char* what, bool f32) {
+                 const char* what, bool f32, Map16 type16 = Map16::kBits) {
     std::call_once(g_encode_once, []() {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -177,8 +177,12 @@ int encode_tiled(CUtensorMap* map, int rank, const void* base, const uint64_t* d
             gstrides[i - 1] = strides_bytes[i - 1];
         }
     }
-    CUresult r = g_encode(map,
-                          f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+    const CUtensorMapDataType dt =
+        f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+            : (type16 == Map16::kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                      : (type16 == Map16::kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                               : CU_TENSOR_MAP_DATA_TYPE_UINT16));
+    CUresult r = g_encode(map, dt,
                           static_cast<cuuint32_t>(rank), const_cast<void*>(base), gdims, gstrides,
                           gbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -234,7 +238,7 @@ int view_of(const char* fn, const char* name, const cfk_view* user, int64_t N, i
 }
 
 int make_tmap_rows(CUtensorMap* map, const void* base, const RowView& v, uint64_t d,
-                   uint32_t box_rows, int swizzle_bytes, const char* what) {
+                   uint32_t box_rows, int swizzle_bytes, const char* what, Map16 type) {
     // dims (D, S, H, N); a dimension of extent 1 gets a harmless stride (its index is always 0)
     const uint64_t dims[4] = {d, static_cast<uint64_t>(v.S), static_cast<uint64_t>(v.H),
                               static_cast<uint64_t>(v.N)};
@@ -243,7 +247,7 @@ int make_tmap_rows(CUtensorMap* map, const void* base, const RowView& v, uint64_
                                  v.H > 1 ? 2 * static_cast<uint64_t>(v.h) : fallback,
                                  v.N > 1 ? 2 * static_cast<uint64_t>(v.b) : fallback};
     const uint32_t box[4] = {static_cast<uint32_t>(d), box_rows, 1, 1};
-    return encode_tiled(map, 4, base, dims, strides, box, swizzle_bytes, what, false);
+    return encode_tiled(map, 4, base, dims, strides, box, swizzle_bytes, what, false, type);
 }
 
 } // namespace cfk

@@ -69,10 +69,16 @@ inline bool is_packed(const RowView& v, int64_t D) {
 int view_of(const char* fn, const char* name, const cfk_view* user, int64_t N, int64_t H,
             int64_t S, int64_t D, RowView* out);
 
+// Element type a 16-bit tensor map declares: raw 16-bit words (loads and stores, where the type
+// does not matter), or bf16 / f16 for a map that TMA reduce-adds into (the add needs the float
+// type; an integer 16-bit add is not an operation the TMA unit has).
+enum class Map16 { kBits, kBF16, kF16 };
+
 // TMA descriptor over a RowView: dims (D, S, H, N), box D x box_rows x 1 x 1, 16-bit elements,
-// out-of-bounds rows read as zero.
+// out-of-bounds rows read as zero (and are not written by stores or reductions).
 int make_tmap_rows(CUtensorMap* map, const void* base, const RowView& v, uint64_t d,
-                   uint32_t box_rows, int swizzle_bytes, const char* what);
+                   uint32_t box_rows, int swizzle_bytes, const char* what,
+                   Map16 type = Map16::kBits);
 
 // Argument checks shared by the attention entry points (dtype code, ranks, D in {8,16,32,64}).
 int check_attn_args(const char* fn, int dtype, int64_t N, int64_t H, int64_t Sq, int64_t Sk,

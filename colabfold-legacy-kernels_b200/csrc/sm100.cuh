@@ -257,6 +257,16 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const 
                  : "memory");
 }
 
+// Rank-4 tiled add-reduction (element type from the map: f32, or f16/bf16 rounded per add).
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* src,
+                                                  int32_t c0, int32_t c1, int32_t c2,
+                                                  int32_t c3) {
+    asm volatile("cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group"
+                 " [%0, {%2, %3, %4, %5}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+
 // Bulk (untiled) add-reduction of f32 data from shared into global memory, completed through
 // the bulk async-group of the issuing thread.  Both addresses 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_reduce_add_f32(float* gdst, const void* ssrc,

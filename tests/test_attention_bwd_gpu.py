@@ -95,20 +95,22 @@ def test_bwd_select_path(cuda_device):
     _check(*t, 0.25, "select path")
 
 
-@pytest.mark.parametrize("shape", [(24, 2, 200, 200, 32), (40, 4, 256, 256, 16)])
-def test_bwd_batch_row_ranges(cuda_device, monkeypatch, shape):
-    """Large problems run the main kernel once per range of batch rows (bounding the f32
-    accumulator workspace), dbias summed across the ranges; a small accumulator budget makes a
-    small problem take that path (with batch chunks inside each range): same results as one
-    launch, and the oracle's."""
+@pytest.mark.parametrize("shape", [(24, 2, 200, 200, 32), (40, 4, 256, 256, 16), (6, 2, 130, 70, 8)])
+def test_bwd_overwrites_prefilled_outputs(cuda_device, shape):
+    """Head dims 8-32 add their 16-bit partial sums straight into dq, dk and dv, which the call
+    zeroes first: gradient buffers holding old values (here 7.0, and NaN in dbias) give the same
+    results as fresh ones, and the oracle's."""
+    from colabfold_legacy_kernels import torch_ops
     n, h, sq, sk, d = shape
-    t = _inputs(n, h, sq, sk, d, torch.bfloat16, seed=31 + n)
+    q, k, v, bias, kmask, dout = _inputs(n, h, sq, sk, d, torch.bfloat16, seed=31 + n)
     scale = 1.0 / math.sqrt(d)
-    one = _check(*t, scale, "one range")
-    row_bytes = 4 * h * (sq + 2 * sk) * d
-    monkeypatch.setenv("CFK_BWD_RANGE_BYTES", str(5 * row_bytes))  # 5 rows per range
-    ranged = _check(*t, scale, "ranges of 5 rows")
-    for a, b, name in zip(ranged, one, ("dq", "dk", "dv")):
-        # f32 partial sums reduced in a timing-dependent order: equal up to 16-bit rounding
-        assert_close_bf16(a, b, name + " ranges vs one launch", rtol=1e-2, atol=1e-2)
-    assert_close_f32(ranged[3], one[3], "dbias ranges vs one launch")
+    fresh = _check(q, k, v, bias, kmask, dout, scale, "fresh")
+    out, lse = torch_ops.attention_fwd(q, k, v, bias, kmask, scale)
+    grads = (torch.full_like(q, 7.0), torch.full_like(k, 7.0), torch.full_like(v, 7.0),
+             torch.full((h, sq, sk), float("nan"), dtype=torch.float32, device=q.device))
+    again = torch_ops.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale, grads=grads)
+    torch.cuda.synchronize()
+    for a, b, name in zip(again, fresh, ("dq", "dk", "dv")):
+        # partials reduced in a timing-dependent order: equal up to 16-bit rounding
+        assert_close_bf16(a, b, name + " prefilled vs fresh", rtol=1e-2, atol=1e-2)
+    assert torch.equal(again[3], fresh[3]), "dbias"
