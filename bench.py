@@ -283,10 +283,10 @@ def run_ours(args, rank, world, local_rank):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
     comm = torch.cuda.Stream(dev) if world > 1 else None
 
-    # marks of one eager step: main stream t0 | fwd | rowstat | main | convert | t1, and the
+    # marks of one eager step: main stream t0 | fwd | prep | main | phase2 | t1, and the
     # dbias all-reduce on the comm stream ar0 | ar1 (all timed from t0)
     ev = {name: torch.cuda.Event(enable_timing=True)
-          for name in ("t0", "fwd", "rowstat", "main", "convert", "t1", "ar0", "ar1")}
+          for name in ("t0", "fwd", "prep", "main", "phase2", "t1", "ar0", "ar1")}
 
     main_set = {"q": q, "k": k, "v": v, "dout": dout, "kmask": kmask, "bias": bias, "out": out,
                 "lse": lse, "grads": grads}
@@ -303,13 +303,14 @@ def run_ours(args, rank, world, local_rank):
         torch_ops.attention_bwd(bq, bk, bv, bb, bm, bo, bl, bd, scale, workspace=ws,
                                 grads=bg, phase=0)
         if record:
-            ev["rowstat"].record(stream)
+            ev["prep"].record(stream)
         torch_ops.attention_bwd(bq, bk, bv, bb, bm, bo, bl, bd, scale, workspace=ws,
                                 grads=bg, phase=1)
         if record:
             ev["main"].record(stream)
         if world > 1:
-            # dbias is final after the main kernel: reduce it while the converts run
+            # dbias is final after the main kernel: reduce it while phase 2 runs (head dim 64's
+            # conversion; empty for the head dims <= 32, whose main kernel completes dq, dk, dv)
             comm.wait_stream(stream)
             with torch.cuda.stream(comm):
                 if record:
@@ -320,7 +321,7 @@ def run_ours(args, rank, world, local_rank):
         torch_ops.attention_bwd(bq, bk, bv, bb, bm, bo, bl, bd, scale, workspace=ws,
                                 grads=bg, phase=2)
         if record:
-            ev["convert"].record(stream)
+            ev["phase2"].record(stream)
         if world > 1:
             stream.wait_stream(comm)
         if record:
@@ -383,16 +384,16 @@ def run_ours(args, rank, world, local_rank):
             del graph  # holds NCCL work: released before the process group goes away
     mean = lambda xs: sum(xs) / len(xs) if xs else 0.0
     # per-step phase durations from the marks (eager loop)
-    pairs = {"fwd": (None, "fwd"), "bwd_rowstat": ("fwd", "rowstat"),
-             "bwd_main": ("rowstat", "main"), "bwd_convert": ("main", "convert")}
+    pairs = {"fwd": (None, "fwd"), "bwd_prep": ("fwd", "prep"),
+             "bwd_main": ("prep", "main"), "bwd_phase2": ("main", "phase2")}
     parts = {}
     for name, (a, b) in pairs.items():
         parts[name] = mean([mb - (marks[a][i] if a else 0.0) for i, mb in enumerate(marks[b])])
     if world > 1:
         parts["allreduce"] = mean([e - b for b, e in zip(marks["ar0"], marks["ar1"])])
-        # the part of the all-reduce that the convert does not hide: it ends after the convert
+        # the part of the all-reduce that phase 2 does not hide: it ends after phase 2
         parts["allreduce_exposed"] = mean([max(0.0, e - c) for e, c in
-                                           zip(marks["ar1"], marks["convert"])])
+                                           zip(marks["ar1"], marks["phase2"])])
     ms = mean(marks["t1"])
     ms_graph = mean(graph_ms)
     names = sorted(parts)
@@ -508,8 +509,10 @@ def run_ours(args, rank, world, local_rank):
         "breakdown_ms": dict({k: round(v, 4) for k, v in parts.items()},
                              note="eager step, mean per step, max over ranks; allreduce_exposed "
                                   "= time the dbias all-reduce (comm stream) runs past the end "
-                                  "of the convert it overlaps"),
-        "gpu_launches": 4 * args.steps,  # attn_fwd, rowstat, attn_bwd, f32_to_16 per step
+                                  "of phase 2 (empty at head dim 32); bwd_prep = row statistics "
+                                  "and the zeroing of dq, dk, dv"),
+        # per step: attn_fwd, attn_bwd_prep, the dq/dk/dv zeroing, attn_bwd
+        "gpu_launches": 4 * args.steps,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": me2e, "steps": args.e2e_steps,
                 "overlap": "double-buffered: host->device copies of step i+1 and device->host "
@@ -572,7 +575,7 @@ def bench_attention_views(dev, packed_ms, steps=10):
 
     for _ in range(3):
         step()
-    names = ("fwd", "bwd_rowstat", "bwd_main", "bwd_convert")
+    names = ("fwd", "bwd_prep", "bwd_main", "bwd_phase2")
     ts, parts = [], {k: [] for k in names}
     for _ in range(steps):
         flush.zero_()
@@ -671,7 +674,7 @@ def bench_other_attention(dev, steps=10, world=1, rank=0):
                          "ms": round(ms, 4), "tflops": round(flops / (ms * 1e9), 1),
                          "gflop": round(flops / 1e9, 1)}
         if backward and world > 1:
-            out[cfg.name]["dbias_allreduce"] = "NCCL, %d MB f32, side stream beside the convert" \
+            out[cfg.name]["dbias_allreduce"] = "NCCL, %d MB f32, side stream after the main kernel" \
                 % round(h * s * s * 4 / 1e6, 1)
         del q, k, v, o, lse, fn
         if backward:

@@ -1340,11 +1340,11 @@ BwdWorkspace bwd_workspace(int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t
     return w;
 }
 
-// Phase 0 (bit 1): row statistics of every row.  Phase 1 (bit 2): zero dq, dk, dv (head dims
-// 8-32: the main kernel adds its 16-bit partials straight into them) or the f32 accumulators
-// (head dim 64), run the main kernel and add dbias's batch chunks.  Phase 2 (bit 4): head dim
-// 64 converts its accumulators to 16 bits; nothing for the others.  dbias is final after
-// phase 1, so a caller can reduce it across GPUs while phase 2 runs.
+// Phase 0 (bit 1): row statistics of every row, and dq, dk, dv zeroed (head dims 8-32: the main
+// kernel adds its 16-bit partials straight into them).  Phase 1 (bit 2): zero the f32
+// accumulators (head dim 64), run the main kernel and add dbias's batch chunks.  Phase 2 (bit 4):
+// head dim 64 converts its accumulators to 16 bits; nothing for the others.  dbias is final
+// after phase 1, so a caller can reduce it across GPUs while phase 2 runs.
 template <typename T, int D>
 int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void* k,
                const void* v, const void* bias, const uint8_t* kmask, const void* out,
@@ -1375,16 +1375,28 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
     const int64_t base = static_cast<int64_t>(H) * p.n_it * p.n_jt;
     const int64_t nh = static_cast<int64_t>(N) * H;
 
+    const int64_t rq = nh * Sq * D / 8;
+    const int64_t rkv = nh * Sk * D / 8;
+    const RowStrides out_views[3] = {row_strides(views[5], D), row_strides(views[6], D),
+                                     row_strides(views[7], D)};
     if (phases & 1) {
         attn_bwd_prep_kernel<T, D><<<static_cast<unsigned>(nh * p.n_it), 128, 0, st>>>(
             static_cast<const T*>(out), static_cast<const T*>(dout), lse, stats, Sq, p.n_it, scale,
             kInplace ? 0u : p.mask_bits, row_strides(views[3], D), row_strides(views[4], D));
         CFK_TRY(check_launch("attn_bwd_prep"));
+        if constexpr (!kInplace) {
+            // the outputs (views allowed) the main kernel reduces into
+            const ConvertJob zero{{nullptr, nullptr, nullptr},
+                                  {dq, dk, dv},
+                                  {rq, rkv, rkv},
+                                  {out_views[0], out_views[1], out_views[2]},
+                                  {1.f, 1.f, 1.f},
+                                  {0, 0, 0},
+                                  d8_log2(D)};
+            f32_to_16_kernel<T><<<dev.num_sms * 8, 256, 0, st>>>(zero);
+            CFK_TRY(check_launch("attn_bwd zero"));
+        }
     }
-    const int64_t rq = nh * Sq * D / 8;
-    const int64_t rkv = nh * Sk * D / 8;
-    const RowStrides out_views[3] = {row_strides(views[5], D), row_strides(views[6], D),
-                                     row_strides(views[7], D)};
     if (phases & 2) {
         CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
         CFK_TRY(make_tmap_rows(&tq, q, views[0], D, kBM, G::kSwizzleBytes, "bwd q"));
@@ -1403,17 +1415,8 @@ int launch_bwd(cudaStream_t st, const DeviceInfo& dev, const void* q, const void
             CFK_TRY(make_tmap_3d(&tdv, dv_acc, D, Sk, nh, frow, frow * Sk, C::kPW, kBN, 1,
                                  C::kRowB, "bwd dv acc", true));
         } else {
-            // the outputs themselves (views allowed), zeroed first
-            const ConvertJob zero{{nullptr, nullptr, nullptr},
-                                  {dq, dk, dv},
-                                  {rq, rkv, rkv},
-                                  {out_views[0], out_views[1], out_views[2]},
-                                  {1.f, 1.f, 1.f},
-                                  {0, 0, 0},
-                                  d8_log2(D)};
-            f32_to_16_kernel<T><<<dev.num_sms * 8, 256, 0, st>>>(zero);
-            CFK_TRY(check_launch("attn_bwd zero"));
-            // the maps the reduce-adds go through declare the float type (the add is a float add)
+            // the outputs themselves (zeroed in phase 0); the maps the reduce-adds go through
+            // declare the float type (the add is a float add)
             constexpr Map16 kRed = Elem<T>::kBf16 ? Map16::kBF16 : Map16::kF16;
             CFK_TRY(make_tmap_rows(&tdq, dq, views[5], D, kBM, G::kSwizzleBytes, "bwd dq", kRed));
             CFK_TRY(make_tmap_rows(&tdk, dk, views[6], D, kBN, G::kSwizzleBytes, "bwd dk", kRed));

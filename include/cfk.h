@@ -85,12 +85,13 @@ CFK_API int cfk_attn_bwd(cfk_stream_t stream, cfk_dtype dtype, const void* q, co
                  void* workspace, size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq,
                  int64_t Sk, int64_t D, float scale);
 
-/* The three launches cfk_attn_bwd makes, callable one by one with the same arguments (no
- * counterpart in the reference): phase 0 zeroes the f32 accumulators and computes
- * delta = rowsum(dout * out); phase 1 is the main tcgen05 kernel (it completes dbias); phase 2
- * converts the dq/dk/dv accumulators to dtype.  Issued in order on one stream they equal
- * cfk_attn_bwd; a caller may, for example, start a collective on dbias after phase 1 while
- * phase 2 runs. */
+/* The three stages of cfk_attn_bwd, callable one by one with the same arguments (no
+ * counterpart in the reference): phase 0 computes the row statistics (delta =
+ * rowsum(dout * out), with lse) and, for D <= 32, zeroes dq, dk, dv, into which phase 1 adds
+ * its partial sums; phase 1 is the main tcgen05 kernel (it completes dbias, and for D <= 32
+ * dq, dk, dv); phase 2 converts D = 64's f32 accumulators to dtype (nothing for D <= 32).
+ * Issued in order on one stream they equal cfk_attn_bwd; a caller may, for example, start a
+ * collective on dbias after phase 1 while phase 2 runs. */
 CFK_API int cfk_attn_bwd_phase(int phase, cfk_stream_t stream, cfk_dtype dtype, const void* q,
                        const void* k, const void* v, const void* bias, const uint8_t* kmask,
                        const void* out, const float* lse, const void* dout, void* dq, void* dk,
