@@ -742,6 +742,17 @@ __device__ __forceinline__ void gate_grads2(float2 p, float2 g, float2 dout, flo
     dg = fmul2(fmul2(dp, p), oms);
 }
 
+// gate_grads2 with the sigmoid from one tanh.approx (0.5 tanh(g/2) + 0.5: one MUFU operation
+// instead of an exponential and a reciprocal), for results that are rounded to 16 bits next
+// (the dx pass's dp, dg operands); the weight gradients keep gate_grads2.
+__device__ __forceinline__ void gate_grads2_fast(float2 p, float2 g, float2 dout, float m,
+                                                 float2& dp, float2& dg) {
+    const float2 sg = make_float2(sigmoid_fast(g.x), sigmoid_fast(g.y));
+    dp = fmul2(fmul2(dout, make_float2(m, m)), sg);
+    const float2 oms = ffma2(sg, make_float2(-1.f, -1.f), make_float2(1.f, 1.f));
+    dg = fmul2(fmul2(dp, p), oms);
+}
+
 // bias-row operand of one 128- or 64-column chunk, built in shared memory by one warp:
 // MN-major interleave [16 x cols], row 0 = bias[n0 + n] (0 beyond N), rows 1..15 = 0.
 __device__ __forceinline__ void build_brow(uint16_t* dst, const uint16_t* bias, int n0, int cols,
@@ -1373,9 +1384,10 @@ __global__ void __launch_bounds__(kDxrThreads, 1)
                 for (int e = 0; e < 4; ++e) {
                     const int c = 8 * q + 2 * e;
                     float2 dp2, dg2;
-                    gate_grads2(make_float2(__uint_as_float(pv[c]), __uint_as_float(pv[c + 1])),
-                                make_float2(__uint_as_float(gv[c]), __uint_as_float(gv[c + 1])),
-                                E::to_float2(dw[e]), mk, dp2, dg2);
+                    gate_grads2_fast(
+                        make_float2(__uint_as_float(pv[c]), __uint_as_float(pv[c + 1])),
+                        make_float2(__uint_as_float(gv[c]), __uint_as_float(gv[c + 1])),
+                        E::to_float2(dw[e]), mk, dp2, dg2);
                     op[4 * q + e] = E::pack(dp2.x, dp2.y);
                     og[4 * q + e] = E::pack(dg2.x, dg2.y);
                 }
