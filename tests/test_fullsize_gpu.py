@@ -155,3 +155,65 @@ def test_c4_gdp_full(cuda_device):
             a += b
     for got, exp, name in zip((dwp, dbp, dwg, dbg), acc, ("dwp", "dbp", "dwg", "dbg")):
         assert_close_f32(got, exp, "C4 GDP %s (all rows)" % name)
+
+
+def test_c4_ln_gdp_fused_full(cuda_device):
+    """C4: the LayerNorm-fused GDP forward (cfk_ln_gdp_fwd) on 1,048,576 rows against the
+    oracle's LayerNorm then GDP (sampled rows) and its row statistics (every row)."""
+    from colabfold_legacy_kernels import torch_ops
+    dev = torch.device("cuda", 0)
+    inp = oracle.configs.make_ln_gdp_inputs(oracle.configs.C4, device=dev)
+    z, gamma, beta, eps = inp["x"], inp["gamma"], inp["beta"], inp["eps"]
+    w = [inp[k] for k in ("wp", "bp", "wg", "bg", "mask")]
+    out, mean, rstd = torch_ops.ln_gdp_fwd(z, gamma, beta, eps, *w, return_stats=True)
+    torch.cuda.synchronize()
+    m = z.shape[0]
+    zc, gc, bc = z.cpu(), gamma.cpu(), beta.cpu()
+    wc = [t.cpu() for t in w]
+    sel = torch.cat([torch.arange(0, 256), torch.arange(m - 256, m),
+                     torch.randperm(m, generator=torch.Generator().manual_seed(4))[:3584]])
+    x, _, _ = oracle.layer_norm_fwd(zc[sel], gc, bc, eps)
+    ref = oracle.gdp_fwd(x.to(z.dtype), *wc[:4], wc[4][sel])
+    assert_close_bf16(out.cpu()[sel], ref, "C4 LN+GDP out (sampled rows)")
+    rmean = torch.empty(m, dtype=torch.float64)
+    rrstd = torch.empty(m, dtype=torch.float64)
+    for r0 in range(0, m, 1 << 16):
+        s = slice(r0, r0 + (1 << 16))
+        _, rmean[s], rrstd[s] = oracle.layer_norm_fwd(zc[s], gc, bc, eps)
+    assert_close_f32(mean, rmean, "C4 LN+GDP mean (all rows)")
+    assert_close_f32(rstd, rrstd, "C4 LN+GDP rstd (all rows)")
+
+
+def test_module_scale_projections_full(cuda_device):
+    """The triangle module's projections at C3 size (589,824 rows of C = 128): q|k|v and the
+    gate from one cfk_linear_fwd, dx over the three gradient blocks (dq|dk|dv, dg, the padded
+    bias rows) and their weight/bias gradients, against a plain PyTorch fp32 reference of the
+    same products (sampled rows for y and dx, every row for dw and db)."""
+    from colabfold_legacy_kernels import torch_ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(6)
+    m, c = 768 * 768, 128
+    bf = torch.bfloat16
+    x = torch.randn(m, c, device=dev, generator=g).to(bf)
+    w = (torch.randn(c, 512, device=dev, generator=g) * c ** -0.5).to(bf)
+    b = torch.cat([torch.zeros(384, device=dev), torch.randn(128, device=dev, generator=g)]).to(bf)
+    qkv = torch.empty(m, 384, dtype=bf, device=dev)
+    gate = torch.empty(m, 128, dtype=bf, device=dev)
+    torch_ops.linear_fwd(x, w, b, out=(qkv, gate))
+    dys = [torch.randn(m, n, device=dev, generator=g).to(bf) for n in (384, 128, 16)]
+    ws = [w[:, :384].contiguous(), w[:, 384:].contiguous(),
+          (torch.randn(c, 16, device=dev, generator=g) * c ** -0.5).to(bf)]
+    dx = torch_ops.linear_bwd_dx(dys, ws)
+    grads = torch_ops.linear_bwd_dw(x, dys, [False, True, False])
+    torch.cuda.synchronize()
+    sel = torch.cat([torch.arange(0, 256), torch.arange(m - 256, m),
+                     torch.randperm(m, generator=torch.Generator().manual_seed(5))[:3584]]).to(dev)
+    xf = x.float()
+    ref_y = xf[sel] @ w.float() + b.float()
+    assert_close_bf16(torch.cat([qkv[sel], gate[sel]], 1), ref_y, "projection y (sampled rows)")
+    ref_dx = sum(dy[sel].float() @ wt.float().t() for dy, wt in zip(dys, ws))
+    assert_close_bf16(dx[sel], ref_dx, "projection dx (sampled rows)")
+    for (dw, db), dy, name in zip(grads, dys, ("qkv", "g", "bias")):
+        assert_close_f32(dw, xf.t() @ dy.float(), "dw %s (all rows)" % name)
+        if db is not None:
+            assert_close_f32(db, dy.float().sum(0), "db %s (all rows)" % name)
