@@ -708,6 +708,10 @@ def bench_module(dev, attn_ms, steps=10):
     out = {}
     for ending in (False, True):
         def step():
+            # fresh gradients every step, as a training step with zero_grad(set_to_none=True)
+            # takes them (no accumulation into earlier steps' .grad)
+            m.zero_grad(set_to_none=True)
+            z.grad = None
             m(z, mask, ending=ending).backward(dout)
 
         for _ in range(3):
