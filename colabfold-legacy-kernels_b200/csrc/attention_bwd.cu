@@ -52,7 +52,6 @@
 // Head dim 64 (attn_bwd_inplace_kernel) keeps the first design: its partial-sum buffers need the
 // tensor-memory columns, so P^T and dS^T overwrite S^T and dP^T, the row statistics come from
 // shared memory per score, and the dS warps drain the partials themselves.
-#include <cstdlib>
 #include <type_traits>
 
 #include "attention_common.cuh"
