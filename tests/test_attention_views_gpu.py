@@ -79,11 +79,14 @@ def test_fwd_nshd_layout_fp16(cuda_device):
     assert torch.equal(out, ref) and torch.equal(lse, ref_lse)
 
 
-@pytest.mark.parametrize("d", [16, 32, 64])
-def test_bwd_ending_node_views(cuda_device, d):
-    """Every [N,H,S,D] operand and gradient a view of [S, N, H, D] storage."""
+@pytest.mark.parametrize("d,dtype", [(8, torch.bfloat16), (16, torch.bfloat16),
+                                     (32, torch.bfloat16), (64, torch.bfloat16),
+                                     (32, torch.float16)])
+def test_bwd_ending_node_views(cuda_device, d, dtype):
+    """Every [N,H,S,D] operand and gradient a view of [S, N, H, D] storage (the backward adds
+    its 16-bit partial sums into the dq/dk/dv views through strided TMA maps)."""
     from colabfold_legacy_kernels import torch_ops
-    q, k, v, bias, kmask, dout = _ending_node(4, 2, 190, 250, d, torch.bfloat16, seed=400 + d)
+    q, k, v, bias, kmask, dout = _ending_node(4, 2, 190, 250, d, dtype, seed=400 + d)
     scale = 1.0 / math.sqrt(d)
     out, lse = torch_ops.attention_fwd(q, k, v, bias, kmask, scale, out=_sndh_like(q))
     grads = (_sndh_like(q), _sndh_like(k), _sndh_like(v),
