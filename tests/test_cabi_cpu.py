@@ -191,3 +191,48 @@ def test_noalloc_checks_its_width_before_the_device(libpath):
         cabi.call("cfk_ln_bwd_noalloc", None, cabi.CFK_BF16, None, None, None, None, None, None,
                   None, None, 4, 2048, 1e-5)
     assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT and "1024" in e.value.message
+
+
+def test_linear_arguments_without_device(libpath):
+    """cfk_linear_fwd / cfk_linear_bwd_dx / cfk_linear_bwd_dw(+_workspace_size) reject bad
+    shapes, split points, row strides, segment counts and null buffers before any device
+    call; zero rows of the forward and the dx pass are no-ops."""
+    from colabfold_legacy_kernels import cabi
+    bf = cabi.CFK_BF16
+    with pytest.raises(cabi.CfkError) as e:   # N % 8 != 0
+        cabi.call("cfk_linear_fwd", None, bf, 16, 32, None, 48, 12, None, 0, 12, 4, 64, 12)
+    assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT and "N % 8" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:   # split not at a multiple of 128
+        cabi.call("cfk_linear_fwd", None, bf, 16, 32, None, 48, 100, 64, 156, 100, 4, 64, 256)
+    assert "n_split" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:   # row stride below the row width
+        cabi.call("cfk_linear_fwd", None, bf, 16, 32, None, 48, 8, None, 0, 16, 4, 64, 16)
+    assert "row stride" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_linear_fwd", None, 7, 16, 32, None, 48, 16, None, 0, 16, 4, 64, 16)
+    assert "dtype" in e.value.message
+    assert cabi.call("cfk_linear_fwd", None, bf, None, None, None, None, 16, None, 0, 16,
+                     0, 64, 16) == 0
+    segs = cabi.linear_segs((16, 128, 128, 32, None, None))
+    with pytest.raises(cabi.CfkError) as e:   # no segments
+        cabi.call("cfk_linear_bwd_dx", None, bf, segs, 0, 48, 4, 64)
+    assert "segments" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:   # five segments
+        cabi.call("cfk_linear_bwd_dx", None, bf, cabi.linear_segs(*[(16, 8, 8, 32, None, None)] * 5),
+                  5, 48, 4, 64)
+    assert "segments" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:   # ld < n
+        cabi.call("cfk_linear_bwd_dx", None, bf, cabi.linear_segs((16, 64, 128, 32, None, None)),
+                  1, 48, 4, 64)
+    assert "ld >= n" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:   # no weight for the dx pass
+        cabi.call("cfk_linear_bwd_dx", None, bf, cabi.linear_segs((16, 128, 128, None, None, None)),
+                  1, 48, 4, 64)
+    assert "null" in e.value.message
+    assert cabi.call("cfk_linear_bwd_dx", None, bf, segs, 1, None, 0, 64) == 0
+    with pytest.raises(cabi.CfkError) as e:   # no dw output for the dw pass
+        cabi.call("cfk_linear_bwd_dw", None, bf, 16, segs, 1, 4, 64, None, 0)
+    assert "null" in e.value.message
+    with pytest.raises(cabi.CfkError) as e:
+        cabi.call("cfk_linear_bwd_dw_workspace_size", segs, 1, 4, 64, None)
+    assert "null" in e.value.message
