@@ -46,8 +46,10 @@
 //                warps' next step.
 //   warp 20      TMA producer: per batch row q, dO, k, v tiles, the query tile's statistics
 //                block, and the key-mask operand rows it writes itself.
-//   warp 21      MMA issuer (warps 22, 23 idle: they complete the last warpgroup, which
-//                setmaxnreg needs).
+//   warp 21      score MMA issuer: S'^T and dP'^T of each batch row.
+//   warp 22      partial-sum MMA issuer: dV, dK, dQ of each batch row, so that the next row's
+//                score MMAs never queue behind a wait for the drain (warp 23 idle: it
+//                completes the last warpgroup, which setmaxnreg needs).
 //
 // Head dim 64 (attn_bwd_inplace_kernel) keeps the first design: its partial-sum buffers need the
 // tensor-memory columns, so P^T and dS^T overwrite S^T and dP^T, the row statistics come from
@@ -136,7 +138,8 @@ struct BwdCfg {
     static constexpr int kDsWarps = 16;
     static constexpr int kDrainWarp0 = 16;
     static constexpr int kProducerWarp = 20;
-    static constexpr int kMmaWarp = 21;                // warps 22, 23 complete warpgroup 5
+    static constexpr int kMmaWarp = 21;                // score MMAs
+    static constexpr int kPartWarp = 22;               // partial-sum MMAs (23 idle)
     static constexpr int kThreads = 24 * 32;
     // Registers per thread: 80 at launch (65536 / 768, in units of 8); the dS warpgroups take
     // 96 and the other two give theirs down to 48 (4 x 128 x 96 + 2 x 128 x 48 = 768 x 80).
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     const int n_items_mine = static_cast<int>((p.items - blockIdx.x + gridDim.x - 1) / gridDim.x);
     // Roles by warpgroup, each moving its register share first (setmaxnreg applies to the
     // code it dominates): dS warpgroups 0-3, the drain warpgroup 4, warpgroup 5 = producer,
-    // MMA issuer and two idle warps.
+    // the two MMA issuers and one idle warp.
     const int wgrp = warp >> 2;
     if (wgrp == 5) {
         setmaxnreg_dec<C::kOtherRegs>();
@@ -335,9 +338,13 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
                 break;
             }
         }
-      } else if (warp == C::kMmaWarp) {
-        // =============================== MMA issuer ===============================
-        // The whole warp runs the loop (converged); MMAs and commits are elect.sync-issued.
+      } else if (warp == C::kMmaWarp || warp == C::kPartWarp) {
+        // =============================== MMA issuers ===============================
+        // Each warp runs its loop converged; MMAs and commits are elect.sync-issued.  Warp
+        // kMmaWarp issues the score MMAs of every step, warp kPartWarp the partial-sum MMAs:
+        // each tcgen05.commit tracks the MMAs of its own thread, and the partial sums of step g
+        // are issued only after pds_full(g), which the dS warps signal after sdp_full(g), so the
+        // stage's operands are released (kv_empty) by the partial-sum warp alone.
         constexpr uint32_t kIdS = idesc_f16(128, 128, false, false, E::kBf16);
         constexpr uint32_t kIdExt = idesc_f16(128, 128, false, false, true); // bf16 operands
         constexpr uint32_t kIdPart = idesc_f16(128, G::kDp, false, true, E::kBf16); // A in TMEM
@@ -366,17 +373,17 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             const uint32_t dv_tm = tmem + C::kPartBase;
             const uint32_t dk_tm = dv_tm + G::kDp;
             const uint32_t dq_tm = dv_tm + 2 * G::kDp;
+            // the three accumulators' K-steps interleaved (independent chains)
+            static_assert(kBM == kBN, "one K-step loop for the three partials");
 #pragma unroll
             for (int ks = 0; ks < kBM / 16; ++ks) {
-                // K-step ks = queries [16 ks, +16): warpgroup ks / 2, its half ks % 2
+                // dV, dK: K-step ks = queries [16 ks, +16): warpgroup ks / 2, its half ks % 2
                 const uint32_t col = C::kPStride * (ks >> 1) + 8 * (ks & 1);
                 umma_ts_w(dv_tm, tmem + C::kPCol + col, G::mnmajor(st + C::kOffDO, ks), kIdPart,
                           ks > 0);
                 umma_ts_w(dk_tm, tmem + C::kDSCol + col, G::mnmajor(st + C::kOffQ, ks), kIdPart,
                           ks > 0);
-            }
-#pragma unroll
-            for (int ks = 0; ks < kBN / 16; ++ks) {
+                // dQ: K-step ks = keys [16 ks, +16)
                 const uint64_t da = smem_desc(ds_s + ks * 2048, 16384, 1024, kSwizzle128);
                 umma_ss_w(dq_tm, da, G::mnmajor(st + C::kOffK, ks), kIdDQ, ks > 0);
             }
@@ -385,6 +392,13 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             umma_commit_w(&kv_empty[gp % NST]);
             return true;
         };
+        if (warp == C::kPartWarp) {
+            for (; static_cast<int>(g) < total_steps; ++g) {
+                if (!mbar_wait_w(pds_full, g & 1, abort_flag) || !issue_partials(g)) {
+                    break;
+                }
+            }
+        } else {
         for (int step = 0; step < total_steps; ++step, ++g) {
             const int s = g % NST;
             if (!mbar_wait_w(&kv_full[s], (g / NST) & 1, abort_flag)) {
@@ -396,29 +410,18 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             tc_fence_after();
             const uint32_t st = sbase + C::kOffStages + s * C::kStageBytes;
             const uint64_t bext = ext_desc(st + C::kOffStat);
+            // S'^T and dP'^T K-steps interleaved (independent chains)
 #pragma unroll
             for (int ks = 0; ks < G::kKSteps; ++ks) {
                 umma_ss_w(tmem + C::kSCol, G::kmajor(st + C::kOffK, ks),
                           G::kmajor(st + C::kOffQ, ks), kIdS, ks > 0);
-            }
-            umma_ss_w(tmem + C::kSCol, ext_desc(st + C::kOffAS), bext, kIdExt, 1);
-#pragma unroll
-            for (int ks = 0; ks < G::kKSteps; ++ks) {
                 umma_ss_w(tmem + C::kDPCol, G::kmajor(st + C::kOffV, ks),
                           G::kmajor(st + C::kOffDO, ks), kIdS, ks > 0);
             }
+            umma_ss_w(tmem + C::kSCol, ext_desc(st + C::kOffAS), bext, kIdExt, 1);
             umma_ss_w(tmem + C::kDPCol, adp_desc, bext, kIdExt, 1);
             umma_commit_w(sdp_full);
-            if (g > 0) {
-                if (!mbar_wait_w(pds_full, (g - 1) & 1, abort_flag) || !issue_partials(g - 1)) {
-                    break;
-                }
-            }
         }
-        if (g > 0 && __all_sync(0xffffffffu, *abort_flag == 0)) {
-            if (mbar_wait_w(pds_full, (g - 1) & 1, abort_flag)) {
-                issue_partials(g - 1);
-            }
         }
       }
     } else if (wgrp == 4) {
