@@ -290,6 +290,35 @@ def run_ours(args, rank, world, local_rank):
 
     main_set = {"q": q, "k": k, "v": v, "dout": dout, "kmask": kmask, "bias": bias, "out": out,
                 "lse": lse, "grads": grads}
+    # dbias across ranks: reduce-scatter by query rows (each rank receives the summed rows of its
+    # own residue rows, which is what a row-sharded module back-propagates into its pair rows),
+    # or all-reduce
+    reduce_mode = args.dbias_reduce if world > 1 and N_RES % world == 0 else "all"
+    exchanges = []  # peer-memory exchanges (reduce_mode "peer"), closed at the end
+    if world > 1 and reduce_mode == "peer":
+        from colabfold_legacy_kernels.parallel import PeerDbiasExchange
+        ex = PeerDbiasExchange((HEADS, N_RES, N_RES), dev)
+        exchanges.append(ex)
+        # the backward writes dbias straight into this rank's exchange buffer
+        grads = (grads[0], grads[1], grads[2], ex.dbias)
+        main_set.update(grads=grads, dbias_red=ex.out, exchange=ex)
+    if world > 1 and reduce_mode == "scatter":
+        part = N_RES // world
+        main_set["rs_src"] = torch.empty((world, HEADS, part, N_RES), dtype=torch.float32,
+                                         device=dev)
+        main_set["dbias_red"] = torch.empty((HEADS, part, N_RES), dtype=torch.float32,
+                                            device=dev)
+
+    def reduce_dbias(b):
+        """The cross-rank sum of this step's dbias (comm stream): the rank's query rows into
+        b["dbias_red"], or the whole of it in place."""
+        if reduce_mode == "peer":
+            b["exchange"].reduce_scatter(stream=torch.cuda.current_stream(dev))
+        elif reduce_mode == "scatter":
+            b["rs_src"].copy_(b["grads"][3].view(HEADS, world, part, N_RES).transpose(0, 1))
+            dist.reduce_scatter_tensor(b["dbias_red"].view(-1), b["rs_src"].view(-1))
+        else:
+            dist.all_reduce(b["grads"][3])
 
     def step(record=False, b=main_set):
         stream = torch.cuda.current_stream(dev)
@@ -315,7 +344,7 @@ def run_ours(args, rank, world, local_rank):
             with torch.cuda.stream(comm):
                 if record:
                     ev["ar0"].record(comm)
-                dist.all_reduce(bg[3])
+                reduce_dbias(b)
                 if record:
                     ev["ar1"].record(comm)
         torch_ops.attention_bwd(bq, bk, bv, bb, bm, bo, bl, bd, scale, workspace=ws,
@@ -390,10 +419,10 @@ def run_ours(args, rank, world, local_rank):
     for name, (a, b) in pairs.items():
         parts[name] = mean([mb - (marks[a][i] if a else 0.0) for i, mb in enumerate(marks[b])])
     if world > 1:
-        parts["allreduce"] = mean([e - b for b, e in zip(marks["ar0"], marks["ar1"])])
-        # the part of the all-reduce that phase 2 does not hide: it ends after phase 2
-        parts["allreduce_exposed"] = mean([max(0.0, e - c) for e, c in
-                                           zip(marks["ar1"], marks["phase2"])])
+        parts["dbias_reduce"] = mean([e - b for b, e in zip(marks["ar0"], marks["ar1"])])
+        # the part of the reduction that phase 2 does not hide: it ends after phase 2
+        parts["dbias_reduce_exposed"] = mean([max(0.0, e - c) for e, c in
+                                              zip(marks["ar1"], marks["phase2"])])
     ms = mean(marks["t1"])
     ms_graph = mean(graph_ms)
     names = sorted(parts)
@@ -419,16 +448,22 @@ def run_ours(args, rank, world, local_rank):
                          ("bias", bias))}
     for x, t in (("q", q), ("k", k), ("v", v), ("dout", dout), ("kmask", kmask), ("bias", bias)):
         host[x].copy_(t)
+    # dbias comes back as this rank's reduced result (its rows with the reduce-scatter)
     host_out = {x: torch.empty_like(t, device="cpu").pin_memory()
                 for x, t in (("out", out), ("dq", grads[0]), ("dk", grads[1]), ("dv", grads[2]),
-                             ("dbias", grads[3]))}
+                             ("dbias", main_set.get("dbias_red", grads[3])))}
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = sum(t.numel() * t.element_size() for t in host_out.values())
     # Steps are pipelined over two device buffer sets: step i's host->device copies (one
     # stream) overlap step i-1's compute and step i-2's device->host copies (two more streams);
     # every step still copies all its inputs in and all its results out inside the timed region.
     sets = [main_set, {x: (tuple(torch.empty_like(g) for g in t) if x == "grads"
-                           else torch.empty_like(t)) for x, t in main_set.items()}]
+                           else torch.empty_like(t)) for x, t in main_set.items()
+                       if x != "exchange"}]
+    if reduce_mode == "peer":
+        ex = PeerDbiasExchange((HEADS, N_RES, N_RES), dev)
+        exchanges.append(ex)
+        sets[1].update(grads=sets[1]["grads"][:3] + (ex.dbias,), dbias_red=ex.out, exchange=ex)
     s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     s_comp = torch.cuda.current_stream(dev)
     in_ev = [torch.cuda.Event() for _ in range(2)]
@@ -452,7 +487,8 @@ def run_ours(args, rank, world, local_rank):
             with torch.cuda.stream(s_d2h):
                 s_d2h.wait_event(comp_ev[i % 2])
                 for x, t in (("out", b["out"]), ("dq", b["grads"][0]), ("dk", b["grads"][1]),
-                             ("dv", b["grads"][2]), ("dbias", b["grads"][3])):
+                             ("dv", b["grads"][2]),
+                             ("dbias", b.get("dbias_red", b["grads"][3]))):
                     host_out[x].copy_(t, non_blocking=True)
                 out_ev[i % 2].record(s_d2h)
         s_comp.wait_stream(s_d2h)
@@ -482,6 +518,8 @@ def run_ours(args, rank, world, local_rank):
         h2d, d2h = (int(x) for x in h2d_t.tolist())
     e2e_value = total_flops / (me2e * 1e-3) / 1e12
 
+    for ex in exchanges:  # collective: every rank closes them in the same order
+        ex.close()
     pk = peaks()
     bwd_flops_launch = 8 * n * HEADS * N_RES * N_RES * HEAD_DIM
     achieved = bwd_flops_launch / (ms_bwd * 1e-3) / 1e12
@@ -507,13 +545,24 @@ def run_ours(args, rank, world, local_rank):
                    "head_dim": HEAD_DIM, "rows_per_gpu": n, "parallelism": "rows%d" % world,
                    "l2": "flushed between steps (256 MB write, outside the timed events)",
                    "launch": ("one CUDA graph replay per step (the step captured once, the dbias "
-                              "all-reduce included)" if ms_graph else "eager launches"),
+                              "reduction included)" if ms_graph else "eager launches"),
+                   "dbias_reduction": None if world == 1 else (
+                       "reduce-scatter by query rows (each rank receives the summed dbias rows "
+                       "of its own residue rows) by this library's peer-memory kernel "
+                       "(cfk_dbias_reduce_scatter: CUDA-IPC buffers, one launch reading every "
+                       "rank's rows over NVLink), side stream after the main kernel"
+                       if reduce_mode == "peer" else
+                       "NCCL reduce-scatter by query rows (each rank receives the summed dbias "
+                       "rows of its own residue rows), side stream after the main kernel"
+                       if reduce_mode == "scatter" else
+                       "NCCL all-reduce, side stream after the main kernel"),
                    "eager_ms_per_step": ms_eager},
         "breakdown_ms": dict({k: round(v, 4) for k, v in parts.items()},
-                             note="eager step, mean per step, max over ranks; allreduce_exposed "
-                                  "= time the dbias all-reduce (comm stream) runs past the end "
-                                  "of phase 2 (empty at head dim 32); bwd_prep = row statistics "
-                                  "and the zeroing of dq, dk, dv"),
+                             note="eager step, mean per step, max over ranks; dbias_reduce = the "
+                                  "dbias collective on the comm stream (the reduce-scatter "
+                                  "includes its rank-major gather copy), dbias_reduce_exposed = "
+                                  "the time it runs past the end of phase 2 (empty at head dim "
+                                  "32); bwd_prep = row statistics and the zeroing of dq, dk, dv"),
         # per step: attn_fwd, attn_bwd_prep, the dq/dk/dv zeroing, attn_bwd
         "gpu_launches": 4 * args.steps,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
@@ -531,7 +580,8 @@ def run_ours(args, rank, world, local_rank):
         result["layernorm"] = bench_layernorm(dev, pk)
         result["gdp"] = bench_gdp(dev, pk)
     elif not args.skip_extras:
-        result["other_attention_configs"] = bench_other_attention(dev, world=world, rank=rank)
+        result["other_attention_configs"] = bench_other_attention(dev, world=world, rank=rank,
+                                                                  reduce_mode=args.dbias_reduce)
         result.update(bench_ln_gdp_sharded(dev, pk, world))
     return result
 
@@ -598,18 +648,19 @@ def bench_attention_views(dev, packed_ms, steps=10):
             "l2": "flushed between steps (256 MB write, outside the timed events)"}
 
 
-def bench_other_attention(dev, steps=10, world=1, rank=0):
+def bench_other_attention(dev, steps=10, world=1, rank=0, reduce_mode="all"):
     """BASELINE's other attention configurations, full size: C2 (MSA row attention with pair
     bias, [512, 8, 256, 32], fwd + the three backward launches) and C5 (triangle attention at
     N_res = 2048, forward only).  With N ranks the attention rows are sharded as in the
     headline step (every GPU holds the full bias); C2's per-rank dbias partials are summed by an
-    NCCL all-reduce on a side stream that overlaps the accumulator conversion.  Eager launches,
+    NCCL reduce-scatter by query rows (reduce_mode "scatter") or all-reduce on a side stream
+    after the main kernel.  Eager launches,
     L2 flushed between steps (untimed); whole-job TFLOP/s over the slowest rank's mean step."""
     import torch
     import torch.distributed as dist
     import oracle
     from colabfold_legacy_kernels import torch_ops
-    from colabfold_legacy_kernels.parallel import shard_rows
+    from colabfold_legacy_kernels.parallel import scatter_dbias, shard_rows
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     comm = torch.cuda.Stream(dev) if world > 1 else None
@@ -652,6 +703,12 @@ def bench_other_attention(dev, steps=10, world=1, rank=0):
             ws = torch_ops.attention_bwd_workspace(n, h, s, s, d, dev)
             grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
                      torch.empty((h, s, s), dtype=torch.float32, device=dev))
+            scatter = world > 1 and reduce_mode == "scatter" and s % world == 0
+            ex = None
+            if world > 1 and reduce_mode == "peer" and s % world == 0:
+                from colabfold_legacy_kernels.parallel import PeerDbiasExchange
+                ex = PeerDbiasExchange((h, s, s), dev)
+                grads = grads[:3] + (ex.dbias,)
 
             def fn():
                 stream = torch.cuda.current_stream(dev)
@@ -662,7 +719,12 @@ def bench_other_attention(dev, steps=10, world=1, rank=0):
                 if world > 1:
                     comm.wait_stream(stream)
                     with torch.cuda.stream(comm):
-                        dist.all_reduce(grads[3])
+                        if ex is not None:
+                            ex.reduce_scatter(stream=comm)
+                        elif scatter:
+                            scatter_dbias(grads[3], world, rank)
+                        else:
+                            dist.all_reduce(grads[3])
                 torch_ops.attention_bwd(*args, workspace=ws, grads=grads, phase=2)
                 if world > 1:
                     stream.wait_stream(comm)
@@ -677,8 +739,12 @@ def bench_other_attention(dev, steps=10, world=1, rank=0):
                          "ms": round(ms, 4), "tflops": round(flops / (ms * 1e9), 1),
                          "gflop": round(flops / 1e9, 1)}
         if backward and world > 1:
-            out[cfg.name]["dbias_allreduce"] = "NCCL, %d MB f32, side stream after the main kernel" \
-                % round(h * s * s * 4 / 1e6, 1)
+            out[cfg.name]["dbias_reduction"] = "%s, %d MB f32, side stream after the main " \
+                "kernel" % ("peer-memory reduce-scatter by query rows (cfk_dbias_reduce_scatter)"
+                            if ex is not None else "NCCL reduce-scatter by query rows" if scatter
+                            else "NCCL all-reduce", round(h * s * s * 4 / 1e6, 1))
+            if ex is not None:
+                ex.close()
         del q, k, v, o, lse, fn
         if backward:
             del ws, grads, dout
@@ -950,6 +1016,9 @@ def main():
     ap.add_argument("--ref-rows", type=int, default=0,
                     help="reference arm: attention rows per step (default: all 768)")
     ap.add_argument("--skip-extras", action="store_true", help="skip LayerNorm/GDP lines")
+    ap.add_argument("--dbias-reduce", choices=("peer", "scatter", "all"), default="peer",
+                    help="N > 1: dbias reduce-scatter by query rows through this library's "
+                         "peer-memory kernel (default) or NCCL, or an NCCL all-reduce")
     ap.add_argument("--no-graph", action="store_true",
                     help="time the eager step only (no CUDA-graph replay)")
     ap.add_argument("--skip-cpu", action="store_true", help="skip the cpu_baseline sample")

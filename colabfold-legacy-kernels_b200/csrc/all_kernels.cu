@@ -11,3 +11,4 @@
 #include "gdp.cu"
 #include "gate.cu"
 #include "linear.cu"
+#include "peer.cu"

@@ -67,7 +67,8 @@ def linear_segs(*segs):
 
 _segs = ctypes.POINTER(LinearSeg)
 
-# name -> argtypes (restype is int for all but the two string getters)
+# name -> argtypes (restype is int for all but the two string getters and the entries of
+# _RESTYPES)
 SIGNATURES = {
     "cfk_attn_fwd": [_vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                      _i64, _i64, _i64, _i64, _i64, _f32],
@@ -107,7 +108,17 @@ SIGNATURES = {
     "cfk_set_wait_limit_ns": [ctypes.c_uint64],
     "cfk_get_wait_limit_ns": [ctypes.POINTER(ctypes.c_uint64)],
     "cfk_test_wait_timeout": [_vp, ctypes.c_uint64, _vp],
+    "cfk_dbias_exchange_bytes": [_i64, _i64, _i64],
+    "cfk_ipc_alloc": [_sz, ctypes.POINTER(_vp), _vp],
+    "cfk_ipc_open": [_vp, ctypes.POINTER(_vp)],
+    "cfk_ipc_close": [_vp],
+    "cfk_ipc_free": [_vp],
+    "cfk_dbias_reduce_scatter": [_vp, ctypes.POINTER(_vp), _int, _int, _i64, _i64, _i64, _vp],
 }
+
+_RESTYPES = {"cfk_dbias_exchange_bytes": _sz}
+
+CFK_IPC_HANDLE_BYTES = 64  # include/cfk.h
 
 _lib = None
 _lock = threading.Lock()
@@ -137,7 +148,7 @@ def function(name):
     if fn is None:
         fn = getattr(lib(), name)
         fn.argtypes = SIGNATURES[name]
-        fn.restype = ctypes.c_int
+        fn.restype = _RESTYPES.get(name, ctypes.c_int)
         _bound[name] = fn
     return fn
 

@@ -4,9 +4,19 @@ process per GPU).
 The attention batch axis (MSA sequences for row attention, pair rows for triangle attention) is
 independent: every rank takes a contiguous block of rows with the full bias, runs the forward
 and backward on it, and the per-rank dbias partials (dbias sums over rows) are added with one
-all-reduce.  dq, dk and dv stay row-local.  On GPUs the all-reduce runs on a side stream as soon
-as the backward's main kernel has finished dbias, overlapping the conversion of the dq/dk/dv
-accumulators (the third backward launch).
+collective.  dq, dk and dv stay row-local.  On GPUs the collective runs on a side stream as soon
+as the backward's main kernel has finished dbias, beside the backward's third launch (head
+dim 64's accumulator conversion; empty for head dims up to 32).
+
+The collective is an all-reduce (every rank receives all of dbias) or, with
+dbias_reduce="scatter", a reduce-scatter by query rows: rank r receives the summed dbias rows
+shard_rows(Sq, world, r) of every head.  The pair bias of a triangle or MSA-row attention is a
+projection of the pair representation, bias[h, i, j] from z[i, j], so in a module whose pair
+rows are sharded the same way as the attention rows, rank r needs exactly those dbias rows to
+back-propagate into its own z rows; the reduce-scatter moves half the bytes of the all-reduce.
+With dbias_reduce="peer" the same reduce-scatter runs as this library's own kernel over peer
+memory (PeerDbiasExchange: every rank's dbias in CUDA-IPC memory, one launch that reads its
+rows from every rank over NVLink and adds them in rank order) instead of an NCCL collective.
 
 LayerNorm and the gated dual projection are row-wise too (ShardedLnGdp): x, y, dx, out stay
 row-local, and the parameter gradients (dgamma, dbeta; dwp, dbp, dwg, dbg), which sum over rows,
@@ -16,6 +26,7 @@ The reference is single-device (grid-level parallelism only, cuda/volta_mma_attn
 module is new capability.
 """
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -36,7 +47,8 @@ class ShardResult:
     dq: torch.Tensor
     dk: torch.Tensor
     dv: torch.Tensor
-    dbias: torch.Tensor   # summed over all ranks
+    dbias: torch.Tensor   # summed over all ranks: [H, Sq, Sk], or with dbias_reduce="scatter"
+                          # this rank's query rows [H, Sq / world, Sk]
 
 
 def _default_fwd(q, k, v, bias, kmask, scale):
@@ -44,14 +56,130 @@ def _default_fwd(q, k, v, bias, kmask, scale):
     return torch_ops.attention_fwd(q, k, v, bias, kmask, scale)
 
 
+def scatter_dbias(dbias, world, rank, group=None):
+    """Reduce-scatter of dbias [H, Sq, Sk] by query rows over `group`: returns this rank's rows
+    shard_rows(Sq, world, rank) of the sum over ranks, [H, Sq / world, Sk].  Sq must be a
+    multiple of `world` (equal chunks).  The rows are first gathered rank-major, [world, H,
+    Sq / world, Sk], one copy, so that one collective covers every head."""
+    h, sq, sk = dbias.shape
+    if sq % world:
+        raise ValueError("dbias reduce-scatter needs Sq (%d) to be a multiple of the world "
+                         "size (%d)" % (sq, world))
+    part = sq // world
+    src = dbias.view(h, world, part, sk).transpose(0, 1).contiguous()
+    out = torch.empty((h, part, sk), dtype=dbias.dtype, device=dbias.device)
+    dist.reduce_scatter_tensor(out.view(-1), src.view(-1), group=group)
+    return out
+
+
+class _DeviceBuffer:
+    """A device allocation made outside torch, seen by torch through __cuda_array_interface__
+    (torch.as_tensor wraps it without a copy; the allocation's owner frees it)."""
+
+    def __init__(self, ptr, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(int(x) for x in shape), "typestr": "<f4",
+                                         "data": (int(ptr), False), "version": 3,
+                                         "strides": None}
+
+
+class PeerDbiasExchange:
+    """dbias [H, Sq, Sk] of every rank of `group` in CUDA-IPC memory, and its reduce-scatter by
+    query rows as one kernel over peer memory (cfk_dbias_reduce_scatter).
+
+    `dbias` is this rank's buffer: pass it to the backward as its dbias output.  After the
+    backward, reduce_scatter() (enqueued on `stream`) writes into `out` [H, Sq / world, Sk] the
+    sum over ranks, in rank order, of this rank's query rows; when it completes no peer reads
+    `dbias` any more.  Every rank must create the exchange, call reduce_scatter and close() in
+    the same order (creation and close() are collective on `group`).  One process per GPU;
+    2 <= world <= 8, Sq % world == 0, Sk % 4 == 0."""
+
+    def __init__(self, shape, device, group=None):
+        from . import cabi
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.shape = tuple(int(x) for x in shape)
+        self.device = torch.device(device)
+        h, sq, sk = self.shape
+        if not 2 <= self.world <= 8 or sq % self.world or sk % 4:
+            raise ValueError("PeerDbiasExchange: world %d, dbias %r (2 <= world <= 8, Sq a "
+                             "multiple of the world size, Sk of 4)" % (self.world, self.shape))
+        nbytes = cabi.function("cfk_dbias_exchange_bytes")(h, sq, sk)
+        if nbytes == 0:
+            raise ValueError("PeerDbiasExchange: dbias %r too large" % (self.shape,))
+        self._cabi = cabi
+        with torch.cuda.device(self.device):
+            own = ctypes.c_void_p()
+            handle = ctypes.create_string_buffer(cabi.CFK_IPC_HANDLE_BYTES)
+            cabi.call("cfk_ipc_alloc", nbytes, ctypes.byref(own), handle)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            ptrs = []
+            for r, raw in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(own.value)
+                    continue
+                peer = ctypes.c_void_p()
+                cabi.call("cfk_ipc_open", ctypes.create_string_buffer(raw, len(raw)),
+                          ctypes.byref(peer))
+                ptrs.append(peer.value)
+        self._own = own.value
+        self._ptrs = ptrs
+        self._buffers = (ctypes.c_void_p * self.world)(*ptrs)
+        self.dbias = torch.as_tensor(_DeviceBuffer(self._own, self.shape), device=self.device)
+        self.out = torch.empty((h, sq // self.world, sk), dtype=torch.float32,
+                               device=self.device)
+
+    def reduce_scatter(self, out=None, stream=None):
+        """Enqueues the reduce-scatter of `dbias` into `out` (default: self.out) on `stream`
+        (default: the current stream); returns `out`."""
+        out = self.out if out is None else out
+        if (out.dtype != torch.float32 or not out.is_contiguous() or out.device != self.device
+                or tuple(out.shape) != tuple(self.out.shape)):
+            raise ValueError("reduce_scatter: out must be a contiguous f32 %r tensor on %s"
+                             % (tuple(self.out.shape), self.device))
+        stream = torch.cuda.current_stream(self.device) if stream is None else stream
+        h, sq, sk = self.shape
+        self._cabi.call("cfk_dbias_reduce_scatter", stream.cuda_stream, self._buffers,
+                        self.world, self.rank, h, sq, sk, out.data_ptr())
+        return out
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (collective: every rank calls it
+        after its last reduce_scatter)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for r, ptr in enumerate(self._ptrs):
+                if r != self.rank:
+                    self._cabi.call("cfk_ipc_close", ptr)
+            dist.barrier(group=self.group)  # every peer has unmapped this rank's buffer
+            self.dbias = None
+            self._cabi.call("cfk_ipc_free", self._own)
+        self._own = None
+
+
 class ShardedAttention:
-    """Forward + backward of attention on this rank's rows, dbias all-reduced over `group`.
+    """Forward + backward of attention on this rank's rows, dbias reduced over `group`.
 
     `fwd(q, k, v, bias, kmask, scale) -> (out, lse)` and `bwd(...)` default to the sm_100a
     kernels; tests pass CPU implementations to check the sharding and the reduction alone.
+    `dbias_reduce`: "all" (all-reduce, every rank gets the whole sum), "scatter" (each rank
+    gets the summed rows of its own query-row shard; see the module docstring) or "peer" (the
+    same rows by this library's peer-memory kernel, PeerDbiasExchange; sm_100a kernels only;
+    call close() on every rank when done).
     """
 
-    def __init__(self, group=None, fwd=None, bwd=None):
+    def __init__(self, group=None, fwd=None, bwd=None, dbias_reduce="all"):
+        if dbias_reduce not in ("all", "scatter", "peer"):
+            raise ValueError("dbias_reduce must be 'all', 'scatter' or 'peer', not %r"
+                             % (dbias_reduce,))
+        if dbias_reduce == "peer" and (fwd is not None or bwd is not None):
+            raise ValueError("dbias_reduce='peer' runs the sm_100a kernels only")
+        self._exchange = None
+        self.dbias_reduce = dbias_reduce
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -63,13 +191,30 @@ class ShardedAttention:
     def rows(self, n_rows):
         return shard_rows(n_rows, self.world, self.rank)
 
+    def close(self):
+        """Releases the peer-memory exchange (collective with dbias_reduce='peer')."""
+        if self._exchange is not None:
+            self._exchange.close()
+            self._exchange = None
+
+    def _reduce(self, dbias):
+        """The cross-rank sum of dbias, whole or this rank's query rows."""
+        if self.dbias_reduce == "peer":
+            out = torch.empty((dbias.shape[0], dbias.shape[1] // self.world, dbias.shape[2]),
+                              dtype=torch.float32, device=dbias.device)
+            return self._exchange.reduce_scatter(out)
+        if self.dbias_reduce == "scatter":
+            return scatter_dbias(dbias, self.world, self.rank, self.group)
+        dist.all_reduce(dbias, group=self.group)
+        return dbias
+
     def step(self, q, k, v, bias, kmask, dout, scale):
         """q, k, v, dout, kmask: this rank's rows; bias: full.  Returns a ShardResult."""
         out, lse = self.fwd(q, k, v, bias, kmask, scale)
         if self.bwd is not None:
             dq, dk, dv, dbias = self.bwd(q, k, v, bias, kmask, out, lse, dout, scale)
             if self.world > 1:
-                dist.all_reduce(dbias, group=self.group)
+                dbias = self._reduce(dbias)
         else:
             dq, dk, dv, dbias = self._bwd_overlapped(q, k, v, bias, kmask, out, lse, dout, scale)
         return ShardResult(out, lse, dq, dk, dv, dbias)
@@ -81,23 +226,33 @@ class ShardedAttention:
         if self._ws is None or self._ws.numel() < torch_ops.cabi.workspace_size(
                 "cfk_attn_bwd_workspace_size", n, h, sq, sk, d):
             self._ws = torch_ops.attention_bwd_workspace(n, h, sq, sk, d, q.device)
-        grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
-                 torch.empty((h, sq, sk), dtype=torch.float32, device=q.device))
+        if self.dbias_reduce == "peer" and self.world > 1:
+            if self._exchange is not None and self._exchange.shape != (h, sq, sk):
+                self.close()
+            if self._exchange is None:
+                self._exchange = PeerDbiasExchange((h, sq, sk), q.device, self.group)
+            # the backward writes dbias straight into this rank's exchange buffer
+            dbias_out = self._exchange.dbias
+        else:
+            dbias_out = torch.empty((h, sq, sk), dtype=torch.float32, device=q.device)
+        grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), dbias_out)
         args = (q, k, v, bias, kmask, out, lse, dout, scale)
         torch_ops.attention_bwd(*args, workspace=self._ws, grads=grads, phase=0)
         torch_ops.attention_bwd(*args, workspace=self._ws, grads=grads, phase=1)
+        dbias = grads[3]
         if self.world > 1:
             stream = torch.cuda.current_stream(q.device)
             if self._comm is None:
                 self._comm = torch.cuda.Stream(q.device)
             self._comm.wait_stream(stream)
             with torch.cuda.stream(self._comm):
-                dist.all_reduce(grads[3], group=self.group)
+                dbias = self._reduce(grads[3])
             grads[3].record_stream(self._comm)
+            dbias.record_stream(stream)  # allocated on the comm stream, used on this one
         torch_ops.attention_bwd(*args, workspace=self._ws, grads=grads, phase=2)
         if self.world > 1:
             torch.cuda.current_stream(q.device).wait_stream(self._comm)
-        return grads
+        return grads[0], grads[1], grads[2], dbias
 
 
 def _flat_views(buf, shapes):

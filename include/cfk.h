@@ -257,6 +257,49 @@ CFK_API int cfk_linear_bwd_dw(cfk_stream_t stream, cfk_dtype dtype, const void* 
                       void* workspace, size_t workspace_bytes);
 
 /* ------------------------------------------------------------------------------------------ */
+/* dbias across GPUs over peer memory (no counterpart in the reference, which runs on one     */
+/* device: cuda/volta_mma_attn.cu:295 parallelises over its grid only).                       */
+/* ------------------------------------------------------------------------------------------ */
+
+#define CFK_IPC_HANDLE_BYTES 64
+
+/* Bytes of one rank's exchange buffer for dbias [H, Sq, Sk] f32: dbias itself (rounded up to
+ * 256 bytes) followed by a 128-byte sync block.  0 for a size outside [1, 2^20] per axis. */
+CFK_API size_t cfk_dbias_exchange_bytes(int64_t H, int64_t Sq, int64_t Sk);
+
+/* Allocates `bytes` of device memory on the current device, zeroed, and returns it with its
+ * CUDA IPC handle (CFK_IPC_HANDLE_BYTES bytes) for the other processes of the node.  The only
+ * allocating entry points of the library are this one and cfk_ipc_open: call them at set-up,
+ * outside stream capture (synchronous). */
+CFK_API int cfk_ipc_alloc(size_t bytes, void** dptr, void* handle);
+
+/* Maps another process's cfk_ipc_alloc buffer into this one (on the current device, with peer
+ * access enabled); a process cannot open its own handle. */
+CFK_API int cfk_ipc_open(const void* handle, void** dptr);
+
+/* Unmaps a buffer mapped by cfk_ipc_open. */
+CFK_API int cfk_ipc_close(void* dptr);
+
+/* Frees a buffer from cfk_ipc_alloc (after every peer has unmapped it). */
+CFK_API int cfk_ipc_free(void* dptr);
+
+/* Reduce-scatter of dbias by query rows, for attention rows sharded across `world` GPUs (one
+ * process each).  buffers: host array of `world` device pointers, rank r's exchange buffer
+ * (cfk_dbias_exchange_bytes(H, Sq, Sk) bytes from cfk_ipc_alloc, peers' through cfk_ipc_open);
+ * its first H*Sq*Sk floats hold rank r's partial dbias [H, Sq, Sk] (the dbias output of its
+ * backward, complete before this call on `stream`).  Writes out [H, Sq/world, Sk] = the sum over
+ * ranks, in rank order 0..world-1 (deterministic), of rows [rank*Sq/world, (rank+1)*Sq/world)
+ * of every head.  One kernel reads those rows straight from the peers' buffers over NVLink;
+ * every rank must make the same calls with the same shape in the same order.  When the launch
+ * completes, no peer reads this rank's dbias any more, so it may be overwritten.  The call
+ * number lives in the sync blocks (device memory), so the launch takes no per-call argument.
+ * A wait for another rank gives up after the wait limit and sets 4 in the status word; the
+ * buffers' counters then no longer agree across ranks: allocate new ones.  2 <= world <= 8,
+ * Sq % world == 0, Sk % 4 == 0, out 16-byte aligned, buffers 256-byte aligned. */
+CFK_API int cfk_dbias_reduce_scatter(cfk_stream_t stream, void* const* buffers, int world,
+                                     int rank, int64_t H, int64_t Sq, int64_t Sk, float* out);
+
+/* ------------------------------------------------------------------------------------------ */
 /* Diagnostics (no counterpart in the reference).                                             */
 /* ------------------------------------------------------------------------------------------ */
 
@@ -264,7 +307,8 @@ CFK_API int cfk_linear_bwd_dw(cfk_stream_t stream, cfk_dtype dtype, const void* 
  * the device's wait limit (one second unless cfk_set_wait_limit_ns changed it).  It then
  * records a code in a per-device status word and the kernel returns early instead of hanging;
  * the outputs of every launch that ran while the word was set are undefined.  This reads the
- * word of the current device (0 = no timeout seen; 1 = a barrier wait ran past its limit). */
+ * word of the current device (0 = no timeout seen; bit 1 = a barrier wait ran past its limit;
+ * bit 4 = a wait for another GPU in cfk_dbias_reduce_scatter did). */
 CFK_API int cfk_device_status(uint32_t* code);
 
 /* Clears the status word of the current device. */

@@ -236,3 +236,37 @@ def test_linear_arguments_without_device(libpath):
     with pytest.raises(cabi.CfkError) as e:
         cabi.call("cfk_linear_bwd_dw_workspace_size", segs, 1, 4, 64, None)
     assert "null" in e.value.message
+
+
+def test_dbias_exchange_arguments_without_device(libpath):
+    """The peer-memory dbias reduce-scatter and its IPC helpers check their arguments before
+    they touch a device; the exchange size is dbias rounded up to 256 bytes plus the 128-byte
+    sync block."""
+    from colabfold_legacy_kernels import cabi
+    size = cabi.function("cfk_dbias_exchange_bytes")
+    assert size(4, 768, 768) == 4 * 768 * 768 * 4 + 128
+    assert size(1, 3, 4) == 256 + 128
+    assert size(0, 8, 8) == 0 and size(4, 1 << 21, 8) == 0
+    bufs = (ctypes.c_void_p * 2)(256, 512)
+    out = ctypes.c_void_p(4096)
+    bad = [
+        (None, 2, 0, 4, 8, 8, out),            # no buffers
+        (bufs, 2, 0, 4, 8, 8, None),           # no output
+        (bufs, 1, 0, 4, 8, 8, out),            # one rank
+        (bufs, 9, 0, 4, 8, 8, out),            # more than eight
+        (bufs, 2, 2, 4, 8, 8, out),            # rank outside the world
+        (bufs, 2, 0, 4, 7, 8, out),            # Sq not a multiple of the world size
+        (bufs, 2, 0, 4, 8, 6, out),            # Sk not a multiple of 4
+        (bufs, 2, 0, 4, 8, 8, ctypes.c_void_p(4100)),             # out misaligned
+        ((ctypes.c_void_p * 2)(256, 300), 2, 0, 4, 8, 8, out),    # buffer misaligned
+        ((ctypes.c_void_p * 2)(256, None), 2, 0, 4, 8, 8, out),   # a null buffer
+    ]
+    for b, world, rank, h, sq, sk, o in bad:
+        with pytest.raises(cabi.CfkError) as e:
+            cabi.call("cfk_dbias_reduce_scatter", None, b, world, rank, h, sq, sk, o)
+        assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT, (world, rank, sq, sk)
+    for name, args in (("cfk_ipc_alloc", (16, None, None)), ("cfk_ipc_open", (None, None)),
+                       ("cfk_ipc_close", (None,)), ("cfk_ipc_free", (None,))):
+        with pytest.raises(cabi.CfkError) as e:
+            cabi.call(name, *args)
+        assert e.value.code == cabi.CFK_ERR_INVALID_ARGUMENT

@@ -1,4 +1,5 @@
-"""Row-sharded attention with the dbias all-reduce, on CPU ranks (gloo, world size 2).
+"""Row-sharded attention with the dbias all-reduce or reduce-scatter, on CPU ranks (gloo, world
+size 2).
 
 The sharding and the reduction are host logic; the per-rank compute is the CPU oracle here (the
 GPU path passes the sm_100a kernels instead).  A second test makes one rank fail before the
@@ -34,7 +35,7 @@ def _inputs():
     return q, k, v, bias, kmask, dout, 0.35
 
 
-def _worker(rank, world, port, queue, fail_rank):
+def _worker(rank, world, port, queue, fail_rank, reduce="all"):
     try:
         sys.path[:0] = [REPO, os.path.join(REPO, "colabfold-legacy-kernels_b200", "src")]
         import torch.distributed as dist
@@ -53,15 +54,20 @@ def _worker(rank, world, port, queue, fail_rank):
                 raise RuntimeError("injected failure on rank %d" % rank)
             return list(oracle.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale))
 
-        sa = ShardedAttention(fwd=fwd, bwd=bwd)
+        sa = ShardedAttention(fwd=fwd, bwd=bwd, dbias_reduce=reduce)
         res = sa.step(q[r0:r1], k[r0:r1], v[r0:r1], bias, kmask[r0:r1], dout[r0:r1], scale)
         out, lse = oracle.attention_fwd(q, k, v, bias, kmask, scale)
         ref = oracle.attention_bwd(q, k, v, bias, kmask, out, lse, dout, scale)
+        dbias_ref = ref[3]
+        if reduce == "scatter":  # this rank's query rows of the summed dbias
+            s0, s1 = shard_rows(q.shape[2], world, rank)
+            dbias_ref = ref[3][:, s0:s1]
+            assert tuple(res.dbias.shape) == tuple(dbias_ref.shape), res.dbias.shape
         errs = {
             "dq": float((res.dq - ref[0][r0:r1]).abs().max()),
             "dk": float((res.dk - ref[1][r0:r1]).abs().max()),
             "dv": float((res.dv - ref[2][r0:r1]).abs().max()),
-            "dbias": float((res.dbias - ref[3]).abs().max()),
+            "dbias": float((res.dbias - dbias_ref).abs().max()),
             "out": float((res.out - out[r0:r1]).abs().max()),
         }
         queue.put((rank, "ok", errs))
@@ -70,11 +76,11 @@ def _worker(rank, world, port, queue, fail_rank):
         queue.put((rank, "error", "%s: %s" % (type(e).__name__, e)))
 
 
-def _run(world, fail_rank=None, timeout=120):
+def _run(world, fail_rank=None, timeout=120, reduce="all"):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, queue, fail_rank))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue, fail_rank, reduce))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -100,8 +106,9 @@ def test_row_sharding_covers_all_rows():
             assert max(sizes) - min(sizes) <= 1
 
 
-def test_sharded_step_matches_single_process():
-    results = _run(2)
+@pytest.mark.parametrize("reduce", ["all", "scatter"])
+def test_sharded_step_matches_single_process(reduce):
+    results = _run(2, reduce=reduce)
     for rank in (0, 1):
         status, errs = results[rank]
         assert status == "ok", errs
@@ -187,3 +194,11 @@ def test_sharded_ln_gdp_matches_single_process():
         assert status == "ok", errs
         for name, err in errs.items():
             assert err < (1e-12 if name.endswith("dx") else 1e-6), (rank, name, err)
+
+
+def test_scatter_rejects_uneven_rows():
+    from colabfold_legacy_kernels.parallel import ShardedAttention, scatter_dbias
+    with pytest.raises(ValueError):
+        ShardedAttention(dbias_reduce="sum")
+    with pytest.raises(ValueError, match="multiple of the world size"):
+        scatter_dbias(torch.zeros(2, 9, 4), 2, 0)

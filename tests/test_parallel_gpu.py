@@ -1,6 +1,7 @@
 """Row sharding on two GPUs with NCCL (skipped with fewer than two GPUs).
 
-Attention (ShardedAttention: dbias all-reduced on a side stream) and LayerNorm / GDP
+Attention (ShardedAttention: dbias all-reduced, or reduce-scattered by query rows by NCCL or by
+the library's peer-memory kernel, on a side stream) and LayerNorm / GDP
 (ShardedLnGdp: one all-reduce of the flat parameter-gradient buffer), each rank on its own GPU,
 against the same kernels run on the full batch on one GPU, and against the CPU oracle
 (float64; the all-reduced dbias over both ranks' rows).  Row-local outputs computed
@@ -49,7 +50,7 @@ def _worker(rank, world, port, queue):
         import torch.distributed as dist
         import oracle
         from colabfold_legacy_kernels import torch_ops
-        from colabfold_legacy_kernels.parallel import ShardedAttention, ShardedLnGdp
+        from colabfold_legacy_kernels.parallel import ShardedAttention, ShardedLnGdp, shard_rows
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", init_method="tcp://127.0.0.1:%d" % port, rank=rank,
@@ -76,6 +77,40 @@ def _worker(rank, world, port, queue):
         errs["attn_dv_bf"] = float((res.dv.float() - dv[r0:r1].float()).abs().max()
                                    / dv.float().abs().max())
         errs["attn_dbias_rel"] = float((res.dbias - db).abs().max() / db.abs().max())
+        # the same step with dbias reduce-scattered by query rows: this rank's rows of the sum
+        res_rs = ShardedAttention(dbias_reduce="scatter").step(
+            *(t[x][r0:r1] for x in ("q", "k", "v")), t["bias"], t["kmask"][r0:r1],
+            t["dout"][r0:r1], t["scale"])
+        s0, s1 = shard_rows(t["q"].shape[2], world, rank)
+        torch.cuda.synchronize()
+        assert tuple(res_rs.dbias.shape) == (db.shape[0], s1 - s0, db.shape[2])
+        errs["attn_dbias_scatter_rel"] = float((res_rs.dbias - db[:, s0:s1]).abs().max()
+                                               / db.abs().max())
+        # ... and by this library's peer-memory kernel (CUDA-IPC buffers, rows read over
+        # NVLink, added in rank order): two steps in a row, then the exchange alone replayed
+        # twice from a CUDA graph; each must equal the NCCL reduce-scatter (two ranks: one
+        # addition, the same in either order)
+        from colabfold_legacy_kernels import cabi
+        sa_peer = ShardedAttention(dbias_reduce="peer")
+        for call in (1, 2):
+            res_peer = sa_peer.step(*(t[x][r0:r1] for x in ("q", "k", "v")), t["bias"],
+                                    t["kmask"][r0:r1], t["dout"][r0:r1], t["scale"])
+            torch.cuda.synchronize()
+            errs["attn_dbias_peer%d_rel" % call] = float(
+                (res_peer.dbias - res_rs.dbias).abs().max() / db.abs().max())
+        ex = sa_peer._exchange
+        replay_out = torch.full_like(ex.out, float("nan"))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ex.reduce_scatter(out=replay_out)
+        for call in (1, 2):
+            graph.replay()
+            torch.cuda.synchronize()
+            errs["attn_dbias_peer_graph%d_rel" % call] = float(
+                (replay_out - res_rs.dbias).abs().max() / db.abs().max())
+        del graph
+        errs["peer_status_rel"] = float(cabi.device_status())
+        sa_peer.close()
         # the sharded results against the CPU oracle (float64): this rank's rows, and dbias
         # summed over both ranks' rows by the all-reduce
         c = {x: t[x].cpu() for x in ("q", "k", "v", "bias", "kmask", "dout")}
