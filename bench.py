@@ -6,8 +6,10 @@ Workload (BASELINE.json metric "tri-attn fwd+bwd TFLOP/s @N_res=768 ..."): one s
 triangle-attention (starting node) forward + backward with pair bias and key mask at
 N_res = 768, H = 4, d = 32, bf16 (config C3): out, lse = attn_fwd(q, k, v, bias, kmask);
 dq, dk, dv, dbias = attn_bwd(...).  The 768 attention rows are sharded across the N GPUs
-(strong scaling); every GPU holds the full bias and the per-GPU dbias partials are summed with
-one NCCL all-reduce per step.  Inputs are synthetic, drawn from seeded generators with the
+(strong scaling); every GPU holds the full bias and the per-GPU dbias partials are summed once
+per step, by default reduce-scattered by query rows with the library's peer-memory kernel
+(cfk_dbias_reduce_scatter; --dbias-reduce scatter|all for NCCL's reduce-scatter or
+all-reduce).  Inputs are synthetic, drawn from seeded generators with the
 configuration's shapes and distributions (oracle/configs.py), and resident in HBM.
 
 value      = 695.8 GFLOP (algorithmic fwd+bwd flops of the whole job) / ms_per_step
@@ -284,7 +286,7 @@ def run_ours(args, rank, world, local_rank):
     comm = torch.cuda.Stream(dev) if world > 1 else None
 
     # marks of one eager step: main stream t0 | fwd | prep | main | phase2 | t1, and the
-    # dbias all-reduce on the comm stream ar0 | ar1 (all timed from t0)
+    # dbias reduction on the comm stream ar0 | ar1 (all timed from t0)
     ev = {name: torch.cuda.Event(enable_timing=True)
           for name in ("t0", "fwd", "prep", "main", "phase2", "t1", "ar0", "ar1")}
 
@@ -380,7 +382,7 @@ def run_ours(args, rank, world, local_rank):
         wall = time.perf_counter() - wall0
         graph_ms = []
         if not args.no_graph:
-            # The same step captured once in a CUDA graph (the dbias all-reduce included) and
+            # The same step captured once in a CUDA graph (the dbias reduction included) and
             # replayed: the host's per-launch work leaves the timed region, which matters when
             # a step is short (many GPUs).  W warm-up replays, then K timed ones, L2 flushed
             # between them as above.
