@@ -299,11 +299,14 @@ def run_ours(args, rank, world, local_rank):
     exchanges = []  # peer-memory exchanges (reduce_mode "peer"), closed at the end
     if world > 1 and reduce_mode == "peer":
         from colabfold_legacy_kernels.parallel import PeerDbiasExchange
-        ex = PeerDbiasExchange((HEADS, N_RES, N_RES), dev)
-        exchanges.append(ex)
-        # the backward writes dbias straight into this rank's exchange buffer
-        grads = (grads[0], grads[1], grads[2], ex.dbias)
-        main_set.update(grads=grads, dbias_red=ex.out, exchange=ex)
+        ex = PeerDbiasExchange.create_or_none((HEADS, N_RES, N_RES), dev)
+        if ex is None:  # CUDA IPC unavailable on some rank: every rank uses NCCL instead
+            reduce_mode = "scatter"
+        else:
+            exchanges.append(ex)
+            # the backward writes dbias straight into this rank's exchange buffer
+            grads = (grads[0], grads[1], grads[2], ex.dbias)
+            main_set.update(grads=grads, dbias_red=ex.out, exchange=ex)
     if world > 1 and reduce_mode == "scatter":
         part = N_RES // world
         main_set["rs_src"] = torch.empty((world, HEADS, part, N_RES), dtype=torch.float32,
@@ -463,7 +466,9 @@ def run_ours(args, rank, world, local_rank):
                            else torch.empty_like(t)) for x, t in main_set.items()
                        if x != "exchange"}]
     if reduce_mode == "peer":
-        ex = PeerDbiasExchange((HEADS, N_RES, N_RES), dev)
+        ex = PeerDbiasExchange.create_or_none((HEADS, N_RES, N_RES), dev)
+        if ex is None:
+            raise RuntimeError("the second peer-memory exchange could not be set up")
         exchanges.append(ex)
         sets[1].update(grads=sets[1]["grads"][:3] + (ex.dbias,), dbias_red=ex.out, exchange=ex)
     s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -709,8 +714,11 @@ def bench_other_attention(dev, steps=10, world=1, rank=0, reduce_mode="all"):
             ex = None
             if world > 1 and reduce_mode == "peer" and s % world == 0:
                 from colabfold_legacy_kernels.parallel import PeerDbiasExchange
-                ex = PeerDbiasExchange((h, s, s), dev)
-                grads = grads[:3] + (ex.dbias,)
+                ex = PeerDbiasExchange.create_or_none((h, s, s), dev)
+                if ex is None:  # every rank falls back to NCCL together
+                    scatter = True
+                else:
+                    grads = grads[:3] + (ex.dbias,)
 
             def fn():
                 stream = torch.cuda.current_stream(dev)

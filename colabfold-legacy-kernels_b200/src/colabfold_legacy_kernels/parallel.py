@@ -108,27 +108,69 @@ class PeerDbiasExchange:
         if nbytes == 0:
             raise ValueError("PeerDbiasExchange: dbias %r too large" % (self.shape,))
         self._cabi = cabi
-        with torch.cuda.device(self.device):
-            own = ctypes.c_void_p()
-            handle = ctypes.create_string_buffer(cabi.CFK_IPC_HANDLE_BYTES)
-            cabi.call("cfk_ipc_alloc", nbytes, ctypes.byref(own), handle)
-            handles = [None] * self.world
-            dist.all_gather_object(handles, handle.raw, group=group)
-            ptrs = []
-            for r, raw in enumerate(handles):
-                if r == self.rank:
-                    ptrs.append(own.value)
-                    continue
-                peer = ctypes.c_void_p()
-                cabi.call("cfk_ipc_open", ctypes.create_string_buffer(raw, len(raw)),
-                          ctypes.byref(peer))
-                ptrs.append(peer.value)
+        # every rank takes part in the one gather below, also when its allocation failed, so
+        # that the ranks' collectives stay matched; then all of them raise or none does
+        own = ctypes.c_void_p()
+        raw = None
+        try:
+            with torch.cuda.device(self.device):
+                handle = ctypes.create_string_buffer(cabi.CFK_IPC_HANDLE_BYTES)
+                cabi.call("cfk_ipc_alloc", nbytes, ctypes.byref(own), handle)
+                raw = handle.raw
+        except Exception:
+            raw = None
+        handles = [None] * self.world
+        dist.all_gather_object(handles, raw, group=group)
+        failed = [r for r, h in enumerate(handles) if h is None]
+        ptrs = []
+        try:
+            if failed:
+                raise RuntimeError("PeerDbiasExchange: rank(s) %s could not allocate" % failed)
+            with torch.cuda.device(self.device):
+                for r, h in enumerate(handles):
+                    if r == self.rank:
+                        ptrs.append(own.value)
+                        continue
+                    peer = ctypes.c_void_p()
+                    cabi.call("cfk_ipc_open", ctypes.create_string_buffer(h, len(h)),
+                              ctypes.byref(peer))
+                    ptrs.append(peer.value)
+        except Exception:
+            # undo this rank's part (no collective: the other ranks may have succeeded)
+            for r, ptr in enumerate(ptrs):
+                if r != self.rank:
+                    cabi.call("cfk_ipc_close", ptr)
+            if own.value:
+                cabi.call("cfk_ipc_free", own.value)
+            raise
         self._own = own.value
         self._ptrs = ptrs
         self._buffers = (ctypes.c_void_p * self.world)(*ptrs)
         self.dbias = torch.as_tensor(_DeviceBuffer(self._own, self.shape), device=self.device)
         self.out = torch.empty((h, sq // self.world, sk), dtype=torch.float32,
                                device=self.device)
+
+    @classmethod
+    def create_or_none(cls, shape, device, group=None):
+        """An exchange on every rank, or None on every rank when any rank could not set its
+        part up (CUDA IPC unavailable, a mapping refused, ...), so that the ranks agree on
+        which reduction they run.  Collective on `group`."""
+        ex = None
+        try:
+            ex = cls(shape, device, group)
+        except Exception:  # reported through the agreement below
+            ex = None
+        ok = torch.tensor([1 if ex is not None else 0], dtype=torch.int32,
+                          device=torch.device(device))
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 1:
+            return ex
+        if ex is not None:
+            ex._release()
+        dist.barrier(group=group)  # every rank has unmapped its peers' buffers
+        if ex is not None:
+            ex._free_own()
+        return None
 
     def reduce_scatter(self, out=None, stream=None):
         """Enqueues the reduce-scatter of `dbias` into `out` (default: self.out) on `stream`
@@ -151,11 +193,22 @@ class PeerDbiasExchange:
             return
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
+        self._release()
+        dist.barrier(group=self.group)  # every peer has unmapped this rank's buffer
+        self._free_own()
+
+    def _release(self):
+        """Unmaps the peers' buffers (this rank only)."""
         with torch.cuda.device(self.device):
             for r, ptr in enumerate(self._ptrs):
-                if r != self.rank:
+                if r != self.rank and ptr is not None:
                     self._cabi.call("cfk_ipc_close", ptr)
-            dist.barrier(group=self.group)  # every peer has unmapped this rank's buffer
+        self._ptrs = [p if r == self.rank else None for r, p in enumerate(self._ptrs)]
+
+    def _free_own(self):
+        if self._own is None:
+            return
+        with torch.cuda.device(self.device):
             self.dbias = None
             self._cabi.call("cfk_ipc_free", self._own)
         self._own = None
@@ -230,7 +283,11 @@ class ShardedAttention:
             if self._exchange is not None and self._exchange.shape != (h, sq, sk):
                 self.close()
             if self._exchange is None:
-                self._exchange = PeerDbiasExchange((h, sq, sk), q.device, self.group)
+                self._exchange = PeerDbiasExchange.create_or_none((h, sq, sk), q.device,
+                                                                  self.group)
+                if self._exchange is None:  # every rank falls back together
+                    self.dbias_reduce = "scatter"
+        if self._exchange is not None:
             # the backward writes dbias straight into this rank's exchange buffer
             dbias_out = self._exchange.dbias
         else:

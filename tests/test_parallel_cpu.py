@@ -202,3 +202,44 @@ def test_scatter_rejects_uneven_rows():
         ShardedAttention(dbias_reduce="sum")
     with pytest.raises(ValueError, match="multiple of the world size"):
         scatter_dbias(torch.zeros(2, 9, 4), 2, 0)
+
+
+def _exchange_worker(rank, world, port, queue):
+    try:
+        sys.path[:0] = [REPO, os.path.join(REPO, "colabfold-legacy-kernels_b200", "src")]
+        import torch.distributed as dist
+        from colabfold_legacy_kernels.parallel import PeerDbiasExchange
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank,
+                                world_size=world, timeout=timedelta(seconds=15))
+        # no GPU here: every rank's buffer allocation fails, and the ranks agree on "none"
+        # through the collectives instead of some of them waiting for the others
+        ex = PeerDbiasExchange.create_or_none((2, 8, 8), "cpu")
+        try:
+            PeerDbiasExchange((2, 8, 8), "cpu")
+            direct = "no error"
+        except RuntimeError as e:
+            direct = str(e)
+        queue.put((rank, "ok", (ex is None, direct)))
+        dist.destroy_process_group()
+    except Exception as e:
+        queue.put((rank, "error", "%s: %s" % (type(e).__name__, e)))
+
+
+def test_peer_exchange_setup_failure_is_collective():
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict((r, (s, e)) for r, s, e in (queue.get(timeout=120) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    for rank in (0, 1):
+        status, payload = results[rank]
+        assert status == "ok", payload
+        none, direct = payload
+        assert none, rank
+        assert "could not allocate" in direct and "[0, 1]" in direct, direct
