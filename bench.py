@@ -259,6 +259,20 @@ def run_reference(args, rank):
 # ------------------------------------------------------------------------------------------
 # GPU leg
 # ------------------------------------------------------------------------------------------
+def device_status_max(dev, world):
+    """The status word of this device, the largest over the ranks."""
+    import torch
+    import torch.distributed as dist
+    from colabfold_legacy_kernels import cabi
+    torch.cuda.synchronize(dev)
+    code = cabi.device_status()
+    if world > 1:
+        t = torch.tensor([code], dtype=torch.int64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        code = int(t.item())
+    return code
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -579,6 +593,9 @@ def run_ours(args, rank, world, local_rank):
         "roofline": roofline,
         "clocks": clocks.summary(),
         "wall_s_timed": wall,
+        # the per-device status word after the timed work: nonzero if any kernel wait (a barrier
+        # inside a kernel, or a wait for another GPU in the dbias exchange) ran past its limit
+        "device_status": device_status_max(dev, world),
     }
     if world == 1 and not args.skip_extras:
         result["attention_views"] = bench_attention_views(dev, ms_eager)
