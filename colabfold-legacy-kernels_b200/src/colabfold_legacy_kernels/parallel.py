@@ -27,6 +27,7 @@ module is new capability.
 """
 
 import ctypes
+import warnings
 from dataclasses import dataclass
 
 import torch
@@ -121,18 +122,18 @@ class PeerDbiasExchange:
             raw = None
         handles = [None] * self.world
         dist.all_gather_object(handles, raw, group=group)
-        failed = [r for r, h in enumerate(handles) if h is None]
+        failed = [r for r, raw_r in enumerate(handles) if raw_r is None]
         ptrs = []
         try:
             if failed:
                 raise RuntimeError("PeerDbiasExchange: rank(s) %s could not allocate" % failed)
             with torch.cuda.device(self.device):
-                for r, h in enumerate(handles):
+                for r, raw_r in enumerate(handles):
                     if r == self.rank:
                         ptrs.append(own.value)
                         continue
                     peer = ctypes.c_void_p()
-                    cabi.call("cfk_ipc_open", ctypes.create_string_buffer(h, len(h)),
+                    cabi.call("cfk_ipc_open", ctypes.create_string_buffer(raw_r, len(raw_r)),
                               ctypes.byref(peer))
                     ptrs.append(peer.value)
         except Exception:
@@ -158,7 +159,9 @@ class PeerDbiasExchange:
         ex = None
         try:
             ex = cls(shape, device, group)
-        except Exception:  # reported through the agreement below
+        except Exception as e:  # reported here and agreed on below
+            warnings.warn("PeerDbiasExchange: set-up failed on this rank (%s: %s); every rank "
+                          "falls back" % (type(e).__name__, e))
             ex = None
         ok = torch.tensor([1 if ex is not None else 0], dtype=torch.int32,
                           device=torch.device(device))
